@@ -1,0 +1,126 @@
+/*
+ * qattn_b200.h — C ABI of the B200 (sm_100a) tree-verification kernels.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes,
+ * launches asynchronously on the given CUDA stream (a `cudaStream_t` passed
+ * as `void*`; NULL = legacy default stream) and returns a status code:
+ * QA_OK (0) or a negative QA_ERR_* value. Argument errors are detected on the
+ * host before any launch; nothing throws across this boundary. No entry point
+ * allocates device memory unless its comment says so; outputs are caller-owned.
+ *
+ * The Python layer (qattention_b200.ragged_attn) binds these with ctypes and
+ * keeps the reference's operator API (src/ragged_attn.py of QAttention).
+ */
+#ifndef QATTN_B200_H
+#define QATTN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QA_API __attribute__((visibility("default")))
+#else
+#define QA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QA_OK 0
+#define QA_ERR_INVALID (-1)     /* bad size, depth, branching factor, null pointer */
+#define QA_ERR_UNSUPPORTED (-2) /* head_dim / dtype combination not compiled */
+#define QA_ERR_ALIGN (-3)       /* pointer or stride breaks the 16-byte row rule */
+#define QA_ERR_LAUNCH (-4)      /* CUDA launch error (cudaGetLastError) */
+#define QA_ERR_DEVICE (-5)      /* no usable sm_100 device */
+
+#define QA_DTYPE_F16 0
+#define QA_DTYPE_BF16 1
+
+/*
+ * Ancestor-walk attention (tree part of tree verification).
+ *
+ * Replaces the Triton kernels behind
+ *   ragged_attention            src/ragged_attn.py:1080-1166 (kernel :267-387)
+ *   ragged_attention_with_lse   src/ragged_attn.py:499-572   (kernel :401-496)
+ *   ragged_attention_with_parents src/ragged_attn.py:716-795 (kernel :593-713)
+ * and the tree half of ragged_attention_hybrid (src/ragged_attn.py:1851-1888).
+ *
+ * For query token i (sequence-local) of sequence s, head h, the walk visits
+ *   a_0 = i,  a_{t+1} = parent(a_t)   for t = 0 .. max_depth-1,
+ * skipping a step whose node equals the previous step's node, where
+ *   parent(a) = max(a-1, 0) / branching        (parents == NULL)
+ *   parent(a) = parents[cu_q[s] + a]            (explicit; root self-loop)
+ * and computes O = softmax_j(scale * q·K[a_j]) · V[a_j] in fp32.
+ *
+ * Layout: Q/O rows [T_q, Hq, D]; K/V rows [T_kv, Hkv, D] with the innermost
+ * (D) stride 1. KV row of node a of sequence s is
+ *   (cu_kv ? cu_kv[s] : cu_q[s]) + kv_offset + a.
+ * GQA: query head h reads KV head h / (Hq / Hkv).
+ *
+ * Optional outputs/inputs:
+ *   lse        fp32 [T_q, Hq] natural-log LSE of the result (NULL = skip)
+ *   prefix_o / prefix_lse: a previously computed attention result over other
+ *              keys (e.g. the shared prefix). When non-NULL it is merged in
+ *              with the log-sum-exp rule of fused_lse_merge
+ *              (src/ragged_attn.py:1576-1616); O and lse then describe the
+ *              union of both key sets. prefix_o may alias o.
+ */
+typedef struct qa_ancestor_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;                  /* optional */
+  const int32_t* cu_seqlens_q; /* [batch+1], device */
+  const int32_t* cu_seqlens_kv;/* [batch+1], device, optional */
+  const int32_t* parents;      /* [T_q], device, optional */
+  const void* prefix_o;        /* optional, same dtype as o */
+  const float* prefix_lse;     /* optional */
+  int64_t q_stride_t, q_stride_h;
+  int64_t k_stride_t, k_stride_h;
+  int64_t v_stride_t, v_stride_h;
+  int64_t o_stride_t, o_stride_h;
+  int64_t lse_stride_t, lse_stride_h;
+  int64_t prefix_o_stride_t, prefix_o_stride_h;
+  int64_t prefix_lse_stride_t, prefix_lse_stride_h;
+  int32_t batch;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;      /* 32, 64, 128 or 256 */
+  int32_t kv_offset;     /* added to every KV row index (hybrid layout: L) */
+  int32_t branching;     /* >= 1; ignored when parents != NULL */
+  int32_t max_depth;     /* >= 0 */
+  int32_t max_seqlen;    /* >= longest sequence in cu_seqlens_q */
+  float scale;           /* softmax scale, the reference uses 1/sqrt(D) */
+  int32_t dtype;         /* QA_DTYPE_F16 / QA_DTYPE_BF16 */
+} qa_ancestor_args;
+
+QA_API int qa_ancestor_attn(const qa_ancestor_args* args, void* stream);
+
+/*
+ * Two-way log-sum-exp merge. Replaces fused_lse_merge
+ * (src/ragged_attn.py:1619-1653, kernel :1576-1616):
+ *   m = max(la, lb); wa = e^(la-m); wb = e^(lb-m)
+ *   out = (wa*out_a + wb*out_b) / max(wa+wb, 1e-8)
+ * Shapes [B, H, N(, D)] given by strides (elements) for b, h, n; D stride 1.
+ * Unlike the reference it takes permuted views without a .contiguous() copy.
+ */
+QA_API int qa_lse_merge(const float* lse_a, const float* lse_b, const void* out_a,
+                 const void* out_b, void* out, int32_t B, int32_t H, int32_t N,
+                 int32_t head_dim, const int64_t* lse_a_strides /*[3]*/,
+                 const int64_t* lse_b_strides /*[3]*/,
+                 const int64_t* out_a_strides /*[3]*/,
+                 const int64_t* out_b_strides /*[3]*/,
+                 const int64_t* out_strides /*[3]*/, int32_t dtype, void* stream);
+
+/* Human-readable name of a status code (static storage). */
+QA_API const char* qa_status_string(int status);
+
+/* Library version, e.g. "qattn-b200 0.1.0 sm_100a". */
+QA_API const char* qa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QATTN_B200_H */

@@ -1,0 +1,87 @@
+"""ctypes binding of ``libqattn_b200.so`` (the C ABI declared in include/qattn_b200.h).
+
+The library is loaded from this package directory only. There is no fallback:
+if it is missing or fails to load, :func:`lib` raises, so a GPU box without the
+built extension fails loudly instead of silently computing elsewhere.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libqattn_b200.so"
+
+QA_OK = 0
+QA_DTYPE_F16 = 0
+QA_DTYPE_BF16 = 1
+
+# Every symbol the header declares; tests check the library exports all of them.
+EXPORTED = (
+    "qa_ancestor_attn",
+    "qa_lse_merge",
+    "qa_status_string",
+    "qa_version",
+)
+
+
+class AncestorArgs(Structure):
+    """Mirror of ``qa_ancestor_args`` (field order and types must match the header)."""
+
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("o", c_void_p),
+        ("lse", c_void_p),
+        ("cu_seqlens_q", c_void_p), ("cu_seqlens_kv", c_void_p), ("parents", c_void_p),
+        ("prefix_o", c_void_p), ("prefix_lse", c_void_p),
+        ("q_stride_t", c_int64), ("q_stride_h", c_int64),
+        ("k_stride_t", c_int64), ("k_stride_h", c_int64),
+        ("v_stride_t", c_int64), ("v_stride_h", c_int64),
+        ("o_stride_t", c_int64), ("o_stride_h", c_int64),
+        ("lse_stride_t", c_int64), ("lse_stride_h", c_int64),
+        ("prefix_o_stride_t", c_int64), ("prefix_o_stride_h", c_int64),
+        ("prefix_lse_stride_t", c_int64), ("prefix_lse_stride_h", c_int64),
+        ("batch", c_int32), ("num_q_heads", c_int32), ("num_kv_heads", c_int32),
+        ("head_dim", c_int32), ("kv_offset", c_int32), ("branching", c_int32),
+        ("max_depth", c_int32), ("max_seqlen", c_int32),
+        ("scale", c_float), ("dtype", c_int32),
+    ]
+
+
+_LIB = None
+
+
+class QAError(RuntimeError):
+    """A non-zero status returned by the C ABI."""
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH.name} is not built; run `python -m qattention_b200.build` "
+                "(nvcc, sm_100a) before using the CUDA path")
+        L = ctypes.CDLL(str(LIB_PATH))
+        L.qa_ancestor_attn.argtypes = [POINTER(AncestorArgs), c_void_p]
+        L.qa_ancestor_attn.restype = c_int
+        i64p = POINTER(c_int64)
+        L.qa_lse_merge.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                   c_int32, c_int32, c_int32, c_int32,
+                                   i64p, i64p, i64p, i64p, i64p, c_int32, c_void_p]
+        L.qa_lse_merge.restype = c_int
+        L.qa_status_string.argtypes = [c_int]
+        L.qa_status_string.restype = c_char_p
+        L.qa_version.argtypes = []
+        L.qa_version.restype = c_char_p
+        _LIB = L
+    return _LIB
+
+
+def check(status: int, what: str) -> None:
+    if status != QA_OK:
+        msg = lib().qa_status_string(status).decode()
+        raise QAError(f"{what} failed: {msg} (status {status})")
+
+
+def i64_array(vals) -> ctypes.Array:
+    return (c_int64 * len(vals))(*[int(v) for v in vals])

@@ -1,0 +1,95 @@
+// Shared device helpers for the tree-verification kernels (sm_100a only).
+//
+// Element types: fp16 (`__half`) and bf16 (`__nv_bfloat16`) rows are moved as
+// 16-byte vectors (8 elements) and widened to fp32 in registers. All softmax
+// arithmetic is fp32, in log2 units (scores pre-multiplied by scale*log2(e)),
+// and log-sum-exp values leave the kernels in natural-log units, which is the
+// convention of the reference's `lse = m + log(l)`.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qattn_b200.h"
+
+#define QA_DEVINL __device__ __forceinline__
+
+namespace qa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+template <typename T> struct Vec8;
+
+template <> struct Vec8<__half> {
+  QA_DEVINL static void to_f32(const uint4& r, float (&f)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 t = __half22float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  QA_DEVINL static uint4 from_f32(const float (&f)[8]) {
+    uint4 r;
+    __half2* h = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    return r;
+  }
+};
+
+template <> struct Vec8<__nv_bfloat16> {
+  QA_DEVINL static void to_f32(const uint4& r, float (&f)[8]) {
+    // bf16 -> fp32 widening is exact: the bf16 bits are the top half of fp32.
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  QA_DEVINL static uint4 from_f32(const float (&f)[8]) {
+    uint4 r;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    return r;
+  }
+};
+
+// Read-only 16-byte load that is not kept in L1 (rows read exactly once).
+QA_DEVINL uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Read-only 16-byte load through L1 (ancestor rows shared by nearby queries).
+QA_DEVINL uint4 ld_shared_row(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Streaming 16-byte store (output rows are written once and not re-read).
+QA_DEVINL void st_stream(void* p, const uint4& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+QA_DEVINL float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+}  // namespace qa

@@ -1,0 +1,251 @@
+"""Drop-in replacement for QAttention's ``src.ragged_attn`` operator API on B200.
+
+Same function names, arguments, return values and error behaviour as the
+reference module (``src/ragged_attn.py``); the work runs in the hand-written
+sm_100a kernels of ``libqattn_b200.so`` through its C ABI. There is no Triton,
+no dispatch to other backends and no CPU path: CPU tensors raise.
+
+Reference entry points mirrored here (file:line in the reference project):
+  pack_inputs                        src/ragged_attn.py:1054-1077
+  ragged_attention                   src/ragged_attn.py:1080-1166
+  ragged_attention_with_lse          src/ragged_attn.py:499-572
+  ragged_attention_with_parents      src/ragged_attn.py:716-795
+  ragged_attention_sibling(_with_lse) src/ragged_attn.py:1423-1556 (same math)
+  fused_lse_merge                    src/ragged_attn.py:1619-1653
+  ragged_attention_hybrid            src/ragged_attn.py:1851-1888
+"""
+from __future__ import annotations
+
+import math
+from typing import List, Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_SUPPORTED = (torch.float16, torch.bfloat16)
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    return _lib.QA_DTYPE_F16 if dt == torch.float16 else _lib.QA_DTYPE_BF16
+
+
+def _check_qkv(Q, K, V) -> None:
+    # Same assertion and message as the reference (src/ragged_attn.py:1113-1116).
+    assert Q.dtype in _SUPPORTED and Q.dtype == K.dtype == V.dtype, (
+        f"Inputs must be fp16 or bf16 (got {Q.dtype})"
+    )
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor: this library has no CPU path")
+        if t.dim() != 3:
+            raise ValueError(f"{name} must be [tokens, heads, head_dim], got shape {tuple(t.shape)}")
+
+
+def _rowable(t: torch.Tensor) -> torch.Tensor:
+    """Return ``t`` if its rows are 16-byte vectors at 16-byte aligned addresses, else a copy.
+
+    The kernels take arbitrary token/head strides but need stride 1 along
+    head_dim, token/head strides that are multiples of 8 elements and a
+    16-byte aligned base pointer.
+    """
+    ok = (t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:-1])
+          and t.data_ptr() % 16 == 0)
+    return t if ok else t.contiguous()
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _cu_and_max(cu_seqlens: torch.Tensor, max_seqlen: Optional[int], device) -> Tuple[torch.Tensor, int]:
+    """cu_seqlens on the device as int32, and max_seqlen (derived on the host when None).
+
+    Mirrors src/ragged_attn.py:1136-1142: with ``max_seqlen=None`` the offsets
+    are read on the host (a device->host copy if the caller passed a CUDA
+    tensor); pass ``max_seqlen`` and a device ``cu_seqlens`` to stay
+    asynchronous and CUDA-graph capturable.
+    """
+    B = int(cu_seqlens.shape[0]) - 1
+    if max_seqlen is None:
+        cu_cpu = cu_seqlens.cpu()
+        sl = cu_cpu.tolist()
+        max_seqlen = int(max(sl[i + 1] - sl[i] for i in range(B))) if B else 1
+        cu_dev = cu_cpu.to(device=device, dtype=torch.int32, non_blocking=True)
+    else:
+        cu_dev = cu_seqlens.to(device=device, dtype=torch.int32, non_blocking=True)
+    return cu_dev.contiguous(), int(max_seqlen)
+
+
+def pack_inputs(
+    qs: List[torch.Tensor],
+    ks: List[torch.Tensor],
+    vs: List[torch.Tensor],
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Concatenate per-sequence ``[L_i, H, D]`` tensors into the packed ragged layout.
+
+    Returns ``(Q, K, V, cu_seqlens)`` with ``cu_seqlens`` a CPU int32 tensor,
+    ``cu[0] = 0`` and ``cu[i+1] = cu[i] + L_i`` (src/ragged_attn.py:1071-1077).
+    """
+    assert len(qs) == len(ks) == len(vs)
+    B = len(qs)
+    cu_seqlens = torch.zeros(B + 1, dtype=torch.int32)
+    if B:
+        lens = torch.tensor([q.shape[0] for q in qs], dtype=torch.int64)
+        cu_seqlens[1:] = torch.cumsum(lens, 0).to(torch.int32)
+    return torch.cat(qs, 0), torch.cat(ks, 0), torch.cat(vs, 0), cu_seqlens
+
+
+def _ancestor(Q, K, V, cu_dev, max_seqlen, *, branching=1, max_depth=0, parents=None,
+              want_lse=False, cu_kv=None, kv_offset=0, prefix_o=None, prefix_lse=None,
+              out=None, lse_out=None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Launch ``qa_ancestor_attn`` on torch's current stream; returns (O, LSE or None)."""
+    total, Hq, D = Q.shape
+    Hkv = K.shape[1]
+    if K.shape[2] != D or V.shape[1:] != K.shape[1:]:
+        raise ValueError("K/V must be [tokens, kv_heads, head_dim] matching Q's head_dim")
+    if Hq % Hkv != 0:
+        raise ValueError(f"query heads {Hq} must be a multiple of kv heads {Hkv}")
+    if max_depth < 0:
+        raise ValueError(f"max_depth must be >= 0, got {max_depth}")
+    if parents is None and branching < 1:
+        raise ValueError(f"branching_factor must be >= 1, got {branching}")
+    Q, K, V = _rowable(Q), _rowable(K), _rowable(V)
+    O = out if out is not None else torch.empty_like(Q, memory_format=torch.contiguous_format)
+    LSE = lse_out
+    if want_lse and LSE is None:
+        LSE = torch.empty(total, Hq, dtype=torch.float32, device=Q.device)
+    B = int(cu_dev.shape[0]) - 1
+    a = _lib.AncestorArgs()
+    a.q, a.k, a.v, a.o = Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr()
+    a.lse = LSE.data_ptr() if LSE is not None else None
+    a.cu_seqlens_q = cu_dev.data_ptr()
+    a.cu_seqlens_kv = cu_kv.data_ptr() if cu_kv is not None else None
+    a.parents = parents.data_ptr() if parents is not None else None
+    a.q_stride_t, a.q_stride_h = Q.stride(0), Q.stride(1)
+    a.k_stride_t, a.k_stride_h = K.stride(0), K.stride(1)
+    a.v_stride_t, a.v_stride_h = V.stride(0), V.stride(1)
+    a.o_stride_t, a.o_stride_h = O.stride(0), O.stride(1)
+    if LSE is not None:
+        a.lse_stride_t, a.lse_stride_h = LSE.stride(0), LSE.stride(1)
+    if prefix_o is not None:
+        prefix_o = _rowable(prefix_o)
+        a.prefix_o, a.prefix_lse = prefix_o.data_ptr(), prefix_lse.data_ptr()
+        a.prefix_o_stride_t, a.prefix_o_stride_h = prefix_o.stride(0), prefix_o.stride(1)
+        a.prefix_lse_stride_t, a.prefix_lse_stride_h = prefix_lse.stride(0), prefix_lse.stride(1)
+    a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim = B, Hq, Hkv, D
+    a.kv_offset, a.branching, a.max_depth, a.max_seqlen = kv_offset, branching, max_depth, max_seqlen
+    a.scale = 1.0 / math.sqrt(D)
+    a.dtype = _dtype_code(Q.dtype)
+    _lib.check(_lib.lib().qa_ancestor_attn(a, _stream_ptr(Q.device)), "qa_ancestor_attn")
+    return O, LSE
+
+
+def ragged_attention(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    branching_factor: int,
+    max_depth: int,
+    max_seqlen: int = None,
+) -> torch.Tensor:
+    """Ancestor-sparse attention for BFS-ordered complete b-ary draft trees.
+
+    Each query token q attends to {parent^0(q), ..., parent^max_depth(q)} with
+    parent(k) = max(k-1, 0) // b, softmax scale 1/sqrt(D), fp32 accumulation.
+    Q, K, V: packed ``[sum L_i, H, D]`` fp16/bf16 CUDA tensors; returns O like Q.
+    """
+    _check_qkv(Q, K, V)
+    cu_dev, ms = _cu_and_max(cu_seqlens, max_seqlen, Q.device)
+    O, _ = _ancestor(Q, K, V, cu_dev, ms, branching=branching_factor, max_depth=max_depth)
+    return O
+
+
+def ragged_attention_with_lse(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    branching_factor: int,
+    max_depth: int,
+    max_seqlen: int = None,
+) -> tuple:
+    """As :func:`ragged_attention`, also returning ``lse`` fp32 ``[sum L_i, H]``
+    (natural log of the softmax denominator in scaled-score units)."""
+    _check_qkv(Q, K, V)
+    cu_dev, ms = _cu_and_max(cu_seqlens, max_seqlen, Q.device)
+    return _ancestor(Q, K, V, cu_dev, ms, branching=branching_factor, max_depth=max_depth,
+                     want_lse=True)
+
+
+def ragged_attention_with_parents(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    parents: torch.Tensor,
+    max_depth: int,
+    max_seqlen: int = None,
+) -> tuple:
+    """Ancestor-sparse attention over explicit (pruned / EAGLE-style) trees.
+
+    ``parents[global_pos]`` is the sequence-local parent index; roots carry a
+    self-loop ``parents[root] = root``. The walk stops at the first self-loop or
+    after ``max_depth`` parent steps. A parent outside ``[0, L_i)`` also ends
+    the walk (the reference reads out of bounds there). Returns (O, lse).
+    """
+    _check_qkv(Q, K, V)
+    cu_dev, ms = _cu_and_max(cu_seqlens, max_seqlen, Q.device)
+    if parents.shape[0] != Q.shape[0]:
+        raise ValueError(f"parents must have one entry per token ({Q.shape[0]}), got {parents.shape[0]}")
+    par = parents.to(device=Q.device, dtype=torch.int32, non_blocking=True).contiguous()
+    return _ancestor(Q, K, V, cu_dev, ms, parents=par, max_depth=max_depth, want_lse=True)
+
+
+def ragged_attention_sibling(Q, K, V, cu_seqlens, branching_factor, max_depth, max_seqlen=None):
+    """Alias of :func:`ragged_attention`. The reference's sibling kernel
+    (src/ragged_attn.py:1211-1420) only reorders loads of the same math; the
+    B200 kernel already shares ancestor rows between siblings."""
+    return ragged_attention(Q, K, V, cu_seqlens, branching_factor, max_depth, max_seqlen)
+
+
+def ragged_attention_sibling_with_lse(Q, K, V, cu_seqlens, branching_factor, max_depth,
+                                      max_seqlen=None):
+    """Alias of :func:`ragged_attention_with_lse` (see :func:`ragged_attention_sibling`)."""
+    return ragged_attention_with_lse(Q, K, V, cu_seqlens, branching_factor, max_depth, max_seqlen)
+
+
+def fused_lse_merge(
+    lse_pre: torch.Tensor,
+    lse_tree: torch.Tensor,
+    out_pre: torch.Tensor,
+    out_tree: torch.Tensor,
+) -> torch.Tensor:
+    """Merge two partial attention results by log-sum-exp.
+
+    ``lse_*``: ``[B, H, N_q]`` fp32; ``out_*``: ``[B, H, N_q, D]`` fp16/bf16, any
+    strides with a unit head_dim stride (permuted views need no copy).
+    Returns a new contiguous ``[B, H, N_q, D]`` tensor of ``out_pre``'s dtype.
+    """
+    B, H, N_q, D = out_pre.shape
+    for t in (lse_pre, lse_tree, out_pre, out_tree):
+        if not t.is_cuda:
+            raise RuntimeError("fused_lse_merge needs CUDA tensors: this library has no CPU path")
+    if out_tree.dtype != out_pre.dtype:
+        out_tree = out_tree.to(out_pre.dtype)
+    lp, lt = lse_pre.float(), lse_tree.float()
+    op = out_pre if (out_pre.stride(-1) == 1 and out_pre.data_ptr() % 16 == 0
+                     and all(s % 8 == 0 for s in out_pre.stride()[:3])) else out_pre.contiguous()
+    ot = out_tree if (out_tree.stride(-1) == 1 and out_tree.data_ptr() % 16 == 0
+                      and all(s % 8 == 0 for s in out_tree.stride()[:3])) else out_tree.contiguous()
+    res = torch.empty(B, H, N_q, D, dtype=out_pre.dtype, device=out_pre.device)
+    L = _lib.lib()
+    st = L.qa_lse_merge(lp.data_ptr(), lt.data_ptr(), op.data_ptr(), ot.data_ptr(), res.data_ptr(),
+                        B, H, N_q, D,
+                        _lib.i64_array(lp.stride()), _lib.i64_array(lt.stride()),
+                        _lib.i64_array(op.stride()[:3]), _lib.i64_array(ot.stride()[:3]),
+                        _lib.i64_array(res.stride()[:3]), _dtype_code(res.dtype),
+                        _stream_ptr(res.device))
+    _lib.check(st, "qa_lse_merge")
+    return res

@@ -1,0 +1,269 @@
+"""GPU parity of the ancestor-walk kernel against the CPU oracle (reference restatement).
+
+Mirrors the reference suite tests/test_correctness.py:254-350 (72-config sweep,
+benchmark shapes, head dims, single token, linear chain) with the same
+tolerance (atol = rtol = 1e-2 vs an fp32 padded masked SDPA), plus golden
+fixtures produced by the reference itself, LSE, explicit parents, ragged and
+truncated trees, strided views, GQA, bf16 and full-size sliced checks.
+"""
+import itertools
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import tree_attn_oracle as orc
+from tests.golden.make_golden import SDPA_CASES
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 1e-2
+RTOL = 1e-2
+
+if torch.cuda.is_available():
+    from qattention_b200 import ragged_attn as ra
+    from qattention_b200 import tree_mask as tm
+
+
+def _gen(seed, n, H, D, B, dtype=torch.float16):
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda: [torch.randn(n, H, D, generator=g).to(dtype) for _ in range(B)]  # noqa: E731
+    return mk(), mk(), mk()
+
+
+def _check(B, b, d, H, D, dtype=torch.float16):
+    N = tm.num_tree_nodes(b, d)
+    qs, ks, vs = _gen(B * 100 + b * 10 + d, N, H, D, B, dtype)
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    O = ra.ragged_attention(Q.cuda(), K.cuda(), V.cuda(), cu, branching_factor=b, max_depth=d)
+    ref = torch.cat(orc.padded_sdpa(qs, ks, vs, [tm.tree_attention_mask(b, d)] * B), 0)
+    out = O.float().cpu()
+    assert O.dtype == dtype and O.shape == Q.shape
+    err = (out - ref).abs().max().item()
+    assert torch.allclose(out, ref, atol=ATOL, rtol=RTOL), f"B={B} b={b} d={d} peak_abs={err:.3e}"
+    return err
+
+
+@pytest.mark.parametrize("B,b,d", list(itertools.product([1, 2, 4, 8], [1, 2, 3], [1, 2, 3, 4, 5, 6])))
+def test_ragged_vs_sdpa(B, b, d):
+    _check(B, b, d, 4, 64)
+
+
+@pytest.mark.parametrize("B,b,d", [(4, 2, 5), (4, 3, 5), (8, 2, 5), (8, 3, 5), (4, 2, 6), (4, 3, 6)])
+def test_benchmark_configs(B, b, d):
+    _check(B, b, d, 8, 128)
+
+
+@pytest.mark.parametrize("D", [32, 64, 128, 256])
+def test_head_dims(D):
+    _check(4, 2, 3, 4, D)
+
+
+def test_single_token():
+    _check(4, 1, 0, 4, 64)
+
+
+def test_linear_chain():
+    _check(4, 1, 8, 4, 64)
+
+
+@pytest.mark.parametrize("b,d", [(4, 3), (5, 2), (8, 2), (28, 1)])
+def test_wide_trees(b, d):
+    # b > 4 splits siblings into register chunks of 4
+    _check(2, b, d, 4, 64)
+
+
+@pytest.mark.parametrize("b,d", [(2, 4), (3, 3)])
+def test_bf16(b, d):
+    _check(2, b, d, 4, 64, dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", [c[0] for c in SDPA_CASES])
+def test_golden_fixtures(golden, case):
+    c = golden["sdpa_cases"]
+    B, b, d, H, D = (int(x) for x in c[f"{case}_meta"])
+    Q, K, V = (torch.from_numpy(c[f"{case}_{x}"]).cuda() for x in "qkv")
+    cu = torch.from_numpy(c[f"{case}_cu"])
+    O = ra.ragged_attention(Q, K, V, cu, b, d)
+    ref = torch.from_numpy(c[f"{case}_out"]).float()
+    assert torch.allclose(O.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_config1_fp32_inputs(golden):
+    # BASELINE config 1 draws fp32 inputs; the kernel computes from their fp16 cast.
+    c = golden["sdpa_cases"]
+    q, k, v = (torch.from_numpy(c[f"c1_{x}"]) for x in "qkv")
+    cu = torch.tensor([0, q.shape[0]], dtype=torch.int32)
+    O = ra.ragged_attention(q.half().cuda(), k.half().cuda(), v.half().cuda(), cu, 2, 3)
+    ref = torch.from_numpy(c["c1_out"]).float()
+    assert (O.float().cpu() - ref).abs().max().item() <= ATOL
+
+
+def test_lse_matches_oracle():
+    B, b, d, H, D = 3, 3, 4, 4, 64
+    N = tm.num_tree_nodes(b, d)
+    qs, ks, vs = _gen(7, N, H, D, B)
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    O, L = ra.ragged_attention_with_lse(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    ro, rl = orc.sparse_ancestor_attention(Q, K, V, cu, b, d)
+    assert L.dtype == torch.float32 and L.shape == (B * N, H)
+    assert torch.allclose(L.cpu().double(), rl, atol=1e-4)
+    assert torch.allclose(O.float().cpu(), ro.float(), atol=ATOL, rtol=RTOL)
+    O2 = ra.ragged_attention(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    assert torch.equal(O2, O)
+
+
+def test_ragged_lengths_and_truncated_depth():
+    # sequences that are not complete trees, and max_depth below the true depth
+    H, D, b, d = 4, 64, 2, 3
+    lens = [15, 9, 1, 40, 2]
+    g = torch.Generator().manual_seed(3)
+    qs = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    ks = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    vs = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    O, L = ra.ragged_attention_with_lse(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    masks = [orc.ancestor_mask(n, b, d) for n in lens]
+    ref, rl = orc.padded_sdpa(qs, ks, vs, masks, return_lse=True)
+    assert torch.allclose(O.float().cpu(), torch.cat(ref, 0), atol=ATOL, rtol=RTOL)
+    assert torch.allclose(L.cpu(), torch.cat(rl, 0), atol=1e-3)
+
+
+@pytest.mark.parametrize("b,d,target,seed", [(2, 4, None, 11), (3, 4, 30, 12), (4, 5, 60, 13), (1, 6, None, 14)])
+def test_explicit_parents_pruned_trees(b, d, target, seed):
+    H, D, B = 4, 64, 3
+    rng = np.random.default_rng(seed)
+    trees = [tm.build_pruned_tree(b, d, target_nodes=target, rng=rng) for _ in range(B)]
+    g = torch.Generator().manual_seed(seed)
+    qs = [torch.randn(len(t), H, D, generator=g).half() for t in trees]
+    ks = [torch.randn(len(t), H, D, generator=g).half() for t in trees]
+    vs = [torch.randn(len(t), H, D, generator=g).half() for t in trees]
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    parents = torch.from_numpy(np.concatenate([tm.kernel_parents(t) for t in trees]))
+    O, L = ra.ragged_attention_with_parents(Q.cuda(), K.cuda(), V.cuda(), cu, parents, d)
+    masks = [tm.tree_attention_mask_pruned(t) for t in trees]
+    ref, rl = orc.padded_sdpa(qs, ks, vs, masks, return_lse=True)
+    assert torch.allclose(O.float().cpu(), torch.cat(ref, 0), atol=ATOL, rtol=RTOL)
+    assert torch.allclose(L.cpu(), torch.cat(rl, 0), atol=1e-3)
+
+
+def test_parents_path_equals_formula_on_complete_tree():
+    B, b, d, H, D = 2, 3, 4, 4, 64
+    N = tm.num_tree_nodes(b, d)
+    qs, ks, vs = _gen(9, N, H, D, B)
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    par = torch.from_numpy(np.tile(tm.kernel_parents(tm.build_tree(b, d)), B))
+    Of, Lf = ra.ragged_attention_with_lse(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    Op, Lp = ra.ragged_attention_with_parents(Q.cuda(), K.cuda(), V.cuda(), cu, par, d)
+    assert (Of.float() - Op.float()).abs().max().item() <= 2e-3
+    assert (Lf - Lp).abs().max().item() <= 1e-5
+
+
+def test_strided_views_b1_layout():
+    # the E2E caller passes [N, H, D] transposed views of [H, N, D] (scripts/w4a16_e2e.py:1262-1265)
+    b, d, H, D = 2, 4, 8, 128
+    N = tm.num_tree_nodes(b, d)
+    g = torch.Generator().manual_seed(4)
+    base = [torch.randn(H, N, D, generator=g).half().cuda() for _ in range(3)]
+    Qv, Kv, Vv = (t.transpose(0, 1) for t in base)
+    cu = torch.tensor([0, N], dtype=torch.int32)
+    O = ra.ragged_attention(Qv, Kv, Vv, cu, b, d)
+    O_ref = ra.ragged_attention(Qv.contiguous(), Kv.contiguous(), Vv.contiguous(), cu, b, d)
+    assert torch.equal(O, O_ref)
+
+
+def test_gqa_heads():
+    b, d, Hq, Hkv, D, B = 4, 3, 8, 2, 128, 2
+    N = tm.num_tree_nodes(b, d)
+    g = torch.Generator().manual_seed(8)
+    Q = torch.randn(B * N, Hq, D, generator=g).half()
+    K = torch.randn(B * N, Hkv, D, generator=g).half()
+    V = torch.randn(B * N, Hkv, D, generator=g).half()
+    cu = torch.arange(0, (B + 1) * N, N, dtype=torch.int32)
+    O, L = ra._ancestor(Q.cuda(), K.cuda(), V.cuda(), cu.cuda(), N, branching=b, max_depth=d, want_lse=True)
+    ro, rl = orc.sparse_ancestor_attention(Q, K, V, cu, b, d)
+    assert torch.allclose(O.float().cpu(), ro.float(), atol=ATOL, rtol=RTOL)
+    assert torch.allclose(L.cpu().double(), rl, atol=1e-4)
+
+
+def test_fused_lse_merge_permuted_views():
+    B, H, N, D = 2, 4, 37, 64
+    g = torch.Generator().manual_seed(10)
+    lp, lt = torch.randn(B, H, N, generator=g) * 3, torch.randn(B, H, N, generator=g) * 3
+    op = torch.randn(B, N, H, D, generator=g).half()
+    ot = torch.randn(B, H, N, D, generator=g).half()
+    res = ra.fused_lse_merge(lp.cuda(), lt.cuda(), op.cuda().permute(0, 2, 1, 3), ot.cuda())
+    ref = orc.lse_merge(lp, lt, op.permute(0, 2, 1, 3).float(), ot.float())
+    assert res.shape == (B, H, N, D) and res.is_contiguous()
+    assert (res.float().cpu() - ref).abs().max().item() <= 2e-3
+
+
+def test_prefix_merge_fused_in_ancestor_kernel():
+    # ancestor pass seeded with a prefix result == separate passes + LSE merge
+    b, d, H, D, B = 3, 3, 4, 64, 2
+    N = tm.num_tree_nodes(b, d)
+    qs, ks, vs = _gen(12, N, H, D, B)
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    g = torch.Generator().manual_seed(13)
+    po = torch.randn(B * N, H, D, generator=g).half()
+    pl = torch.randn(B * N, H, generator=g) * 2
+    O, L = ra._ancestor(Q.cuda(), K.cuda(), V.cuda(), cu.cuda(), N, branching=b, max_depth=d,
+                        want_lse=True, prefix_o=po.cuda(), prefix_lse=pl.cuda())
+    to, tl = orc.sparse_ancestor_attention(Q, K, V, cu, b, d)
+    ref = orc.lse_merge(pl, tl.float(), po.float(), to.float())
+    assert (O.float().cpu() - ref).abs().max().item() <= ATOL
+    assert torch.allclose(L.cpu().double(), torch.logaddexp(pl.double(), tl), atol=1e-4)
+
+
+def test_batch_permutation_is_bit_exact():
+    # trees are independent: permuting sequences permutes outputs exactly
+    b, d, H, D, B = 2, 5, 8, 128, 4
+    N = tm.num_tree_nodes(b, d)
+    qs, ks, vs = _gen(21, N, H, D, B)
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    O = ra.ragged_attention(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    perm = [2, 0, 3, 1]
+    Q2, K2, V2, _ = ra.pack_inputs([qs[i] for i in perm], [ks[i] for i in perm], [vs[i] for i in perm])
+    O2 = ra.ragged_attention(Q2.cuda(), K2.cuda(), V2.cuda(), cu, b, d)
+    for j, i in enumerate(perm):
+        assert torch.equal(O2[j * N:(j + 1) * N], O[i * N:(i + 1) * N])
+
+
+@pytest.mark.parametrize("cfg", ["C2", "C3"])
+def test_full_size_sliced_against_oracle(cfg):
+    # BASELINE configs 2 and 3 at full size; the oracle checks the first and last tree
+    B, b, d = (8, 4, 5) if cfg == "C2" else (16, 2, 9)
+    H, D = 32, 128
+    N = tm.num_tree_nodes(b, d)
+    g = torch.Generator().manual_seed(2)
+    Q, K, V = (torch.randn(B * N, H, D, generator=g).half() for _ in range(3))
+    cu = torch.arange(0, (B + 1) * N, N, dtype=torch.int32)
+    O, L = ra.ragged_attention_with_lse(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    O, L = O.cpu(), L.cpu()
+    assert torch.isfinite(O.float()).all()
+    for s in (0, B - 1):
+        sl = slice(s * N, (s + 1) * N)
+        ro, rl = orc.sparse_ancestor_attention(Q[sl], K[sl], V[sl], [0, N], b, d, dtype=torch.float32)
+        assert torch.allclose(O[sl].float(), ro, atol=ATOL, rtol=RTOL)
+        assert torch.allclose(L[sl], rl, atol=1e-3)
+
+
+def test_cuda_graph_capture():
+    b, d, H, D, B = 2, 4, 4, 64, 2
+    N = tm.num_tree_nodes(b, d)
+    qs, ks, vs = _gen(31, N, H, D, B)
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    Q, K, V, cud = Q.cuda(), K.cuda(), V.cuda(), cu.cuda()
+    ref = ra.ragged_attention(Q, K, V, cu, b, d)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ra.ragged_attention(Q, K, V, cud, b, d, max_seqlen=N)  # warm-up outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = ra.ragged_attention(Q, K, V, cud, b, d, max_seqlen=N)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
