@@ -4,286 +4,317 @@
 //   _ragged_attn_sparse_kernel      src/ragged_attn.py:267-387  (formula parents)
 //   _ragged_attn_sparse_kernel_lse  src/ragged_attn.py:401-496  (+ LSE)
 //   _ragged_attn_parents_kernel_lse src/ragged_attn.py:593-713  (explicit parents)
-// i.e. FlashAttention-2 online softmax over the query's own row and its
-// ancestors, with the parent rule parent(a) = max(a-1,0)/b applied before the
-// divide (:333-337, :377) and a step skipped when it revisits the previous
-// node (:340). The reference's `l == 0 -> 1` guard (:380) cannot trigger here
-// because every valid query attends at least to itself.
+// i.e. softmax attention of each query over its own row and its ancestors,
+// with the parent rule parent(a) = max(a-1,0)/b applied before the divide
+// (:333-337, :377), max_depth+1 walk steps, and the walk ending where a step
+// would revisit the previous node (:340: root, or a root self-loop in parents
+// mode). The reference's `l == 0 -> 1` guard (:380) cannot trigger: every
+// valid query attends at least to itself.
 //
 // B200 design (not a translation of the Triton tiling):
-//   * Work item = (sequence, sibling group, query head). In a complete b-ary
-//     BFS tree the children of node p are the consecutive nodes
-//     p*b+1 .. p*b+b, and from step 1 on they share every ancestor. One item
-//     holds up to G siblings' queries in registers and streams each shared
-//     ancestor K/V row once for all of them, so on-chip traffic for the
-//     ancestor part drops by G. Own rows (step 0) are read with L1 bypass
-//     since no other item needs them; ancestor rows go through L1/L2.
-//   * D/8 lanes per item, each lane owning 8 contiguous elements (one 16-byte
-//     vector) of the head dimension. Items are ordered head-fastest, so one
-//     warp instruction touches adjacent heads of the same token: contiguous
-//     512 B - 1 KB of the [T, H, D] row-major layout.
-//   * Ancestor indices of the formula mode are pure arithmetic, so the K and V
-//     rows of P ancestor steps are issued back to back before any math
-//     (memory-level parallelism instead of a dependent load chain).
-//   * No tensor cores: the work is a gather with ~2.8 flop per HBM byte.
-//   * No scratch memory, no atomics, no spin-waits.
-#include "qa_common.cuh"
-
-#include <algorithm>
+//   * One CTA = (sequence, query head, tile of MQ consecutive BFS queries),
+//     CTAs ordered head-fastest so concurrently running CTAs stream the same
+//     tokens' rows of all heads (contiguous [T, H, D] memory).
+//   * In a complete b-ary BFS tree the step-s ancestors of a contiguous query
+//     range are the contiguous node range [anc^s(first), anc^s(last)]. The CTA
+//     computes these level ranges, merges overlapping ones into windows, and
+//     stages the tile's Q rows plus every window's K and V rows in shared
+//     memory with 16-byte cp.async copies issued all at once (maximal bytes in
+//     flight, no register cost). Each level s then has one offset with
+//     slot = off[s] + node, so the walk loop addresses shared memory
+//     uniformly: no per-step branches or range checks. Ancestor rows are other
+//     tiles' own rows, so the extra reads hit L2; HBM sees each row once.
+//   * Walk: parent by multiply-high division (no integer divide), q.k and p.v
+//     with sm_100 mixed-precision FMA (16-bit inputs, fp32 accumulation, no
+//     conversions on the fp16 path), and a lazy online softmax that rescales
+//     the running sum only when a score exceeds the reference maximum by more
+//     than 2^8 (the result is exact: only the reference point moves).
+//   * D/16 lanes per query, 16 elements per lane as two 16-byte chunks at
+//     element 8*lane and D/2 + 8*lane (conflict-free shared loads).
+//   * Explicit-parent mode and levels beyond the staged ones (very deep
+//     walks) read ancestor rows from global memory in a second loop.
+//   * No tensor cores (a gather with ~2.8 flop per HBM byte), no global
+//     scratch, no atomics, no spin-waits.
+#include "ancestor_plan.cuh"
 
 namespace qa {
 namespace {
 
+constexpr int kThreads = 256;
+constexpr int kOwnBytes = 16 * 1024;  // Q rows per tile: MQ = kOwnBytes / (2 * D)
+constexpr float kLazy = 8.f;          // rescale threshold, log2 units
+
 struct AncParams {
   qa_ancestor_args a;
-  float scale_log2;  // scale * log2(e)
-  int32_t groups_per_seq;
-  int32_t chunks;    // sibling chunks per parent (formula mode)
+  float scale_log2;   // scale * log2(e)
+  int32_t tiles_per_seq;
   int32_t head_ratio;
-  int64_t total_items;
+  int32_t rows_cap;   // K/V rows of shared memory per CTA
+  FastDiv div_b;      // division by the branching factor
 };
 
-constexpr int kThreads = 256;
-constexpr int kBatch = 4;  // ancestor steps whose rows are loaded together
+template <int D> struct Tile {
+  static constexpr int LPI = D / 16;              // lanes per query
+  static constexpr int QPP = kThreads / LPI;      // queries per pass
+  static constexpr int MQ = kOwnBytes / (2 * D);  // queries per tile
+  static constexpr int RC = D / 8;                // 16-byte chunks per row
+};
 
-template <typename T, int D, int G, bool PARENTS>
-__global__ void __launch_bounds__(kThreads) ancestor_attn_kernel(const AncParams p) {
-  constexpr int LPI = D / 8;            // lanes per item
-  const int lane = threadIdx.x & 31;
-  const int li = lane & (LPI - 1);      // lane within item
-  const unsigned mask =
-      (LPI == 32) ? 0xffffffffu : (((1u << LPI) - 1u) << (lane & ~(LPI - 1)));
-
-  const int64_t item = (int64_t(blockIdx.x) * kThreads + threadIdx.x) / LPI;
-  if (item >= p.total_items) return;
-  const qa_ancestor_args& a = p.a;
-  const int h = int(item % a.num_q_heads);
-  const int64_t rest = item / a.num_q_heads;
-  const int grp = int(rest % p.groups_per_seq);
-  const int seq = int(rest / p.groups_per_seq);
-
-  const int q0 = __ldg(a.cu_seqlens_q + seq);
-  const int len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
-  const int kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
-
-  // ---- which queries this item owns, and their shared first ancestor ----
-  int first, cnt, par;
-  if constexpr (PARENTS) {
-    first = grp;
-    if (first >= len) return;
-    cnt = 1;
-    const int pp = __ldg(a.parents + q0 + first);
-    par = (pp == first || pp < 0 || pp >= len) ? -1 : pp;
-  } else {
-    const int b = a.branching;
-    if (grp == 0) {
-      first = 0;
-      cnt = 1;
-      par = -1;  // root: max(0-1,0)/b == 0 revisits itself
-    } else {
-      const int pg = (grp - 1) / p.chunks;
-      const int c = (grp - 1) - pg * p.chunks;
-      first = pg * b + 1 + c * G;
-      if (first >= len) return;
-      cnt = min(min(G, b - c * G), len - first);
-      par = pg;
-    }
-  }
-  if (a.max_depth == 0) par = -1;
-
-  const int hk = h / p.head_ratio;
-  const T* qb = reinterpret_cast<const T*>(a.q) + int64_t(h) * a.q_stride_h + li * 8;
-  const T* kb = reinterpret_cast<const T*>(a.k) + int64_t(hk) * a.k_stride_h + li * 8;
-  const T* vb = reinterpret_cast<const T*>(a.v) + int64_t(hk) * a.v_stride_h + li * 8;
-
-  // ---- own rows (step 0): Q, K, V of each sibling ----
-  float q[G][8];
-  float m[G], l[G], acc[G][8];
-  uint4 kown[G], vown[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (g < cnt) {
-      const int64_t t = int64_t(q0) + first + g;
-      const int64_t tk = int64_t(kv0) + first + g;
-      uint4 qr = ld_stream(qb + t * a.q_stride_t);
-      kown[g] = ld_stream(kb + tk * a.k_stride_t);
-      vown[g] = ld_stream(vb + tk * a.v_stride_t);
-      Vec8<T>::to_f32(qr, q[g]);
-    } else {
-      kown[g] = vown[g] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) q[g][e] = 0.f;
-    }
-  }
-  // Optional merge source: a prior attention result over other keys, folded in
-  // as one extra "key" whose weight is exp(prefix_lse) and value is prefix_o.
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
-    if (a.prefix_o != nullptr && g < cnt) {
-      const int64_t t = int64_t(q0) + first + g;
-      const float pl = __ldg(a.prefix_lse + t * a.prefix_lse_stride_t +
-                             int64_t(h) * a.prefix_lse_stride_h);
-      if (pl > -INFINITY) {
-        const T* po = reinterpret_cast<const T*>(a.prefix_o) + t * a.prefix_o_stride_t +
-                      int64_t(h) * a.prefix_o_stride_h + li * 8;
-        uint4 pr = ld_stream(po);
-        Vec8<T>::to_f32(pr, acc[g]);
-        m[g] = pl * kLog2e;
-        l[g] = 1.f;
-      }
-    }
-  }
-
-  // step 0 update
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float kf[8], vf[8];
-    Vec8<T>::to_f32(kown[g], kf);
-    float s = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[e], s);
-#pragma unroll
-    for (int off = LPI / 2; off > 0; off >>= 1) s += __shfl_xor_sync(mask, s, off);
-    s *= p.scale_log2;
-    if (g < cnt) {
-      Vec8<T>::to_f32(vown[g], vf);
-      const float mx = fmaxf(m[g], s);
-      const float alpha = fast_exp2(m[g] - mx);
-      const float pr = fast_exp2(s - mx);
-      l[g] = l[g] * alpha + pr;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(pr, vf[e], acc[g][e] * alpha);
-      m[g] = mx;
-    }
-  }
-
-  // ---- shared ancestor steps 1..max_depth, kBatch rows at a time ----
-  int anc = par;
-  int remaining = a.max_depth;
-  while (anc >= 0 && remaining > 0) {
-    int idx[kBatch];
-    bool val[kBatch];
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      val[j] = (anc >= 0) && (j < remaining);
-      idx[j] = anc;
-      if (val[j]) {
-        int nx;
-        if constexpr (PARENTS) {
-          nx = __ldg(a.parents + q0 + anc);
-          if (nx == anc || nx < 0 || nx >= len) nx = -1;
-        } else {
-          nx = (anc == 0) ? -1 : (anc - 1) / a.branching;
-        }
-        anc = nx;
-      }
-    }
-    remaining -= kBatch;
-    uint4 kr[kBatch], vr[kBatch];
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      if (val[j]) {
-        const int64_t tk = int64_t(kv0) + idx[j];
-        kr[j] = ld_shared_row(kb + tk * a.k_stride_t);
-        vr[j] = ld_shared_row(vb + tk * a.v_stride_t);
-      } else {
-        kr[j] = vr[j] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    float sc[G][kBatch];
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      float kf[8];
-      Vec8<T>::to_f32(kr[j], kf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float s = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[e], s);
-        sc[g][j] = s;
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j)
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-#pragma unroll
-        for (int off = LPI / 2; off > 0; off >>= 1)
-          sc[g][j] += __shfl_xor_sync(mask, sc[g][j], off);
-        sc[g][j] = val[j] ? sc[g][j] * p.scale_log2 : -INFINITY;
-      }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float mx = m[g];
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) mx = fmaxf(mx, sc[g][j]);
-      const float alpha = fast_exp2(m[g] - mx);
-      l[g] *= alpha;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
-      m[g] = mx;
-    }
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      float vf[8];
-      Vec8<T>::to_f32(vr[j], vf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float pr = fast_exp2(sc[g][j] - m[g]);  // 0 for masked steps
-        l[g] += pr;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(pr, vf[e], acc[g][e]);
-      }
-    }
-  }
-
-  // ---- epilogue: normalise, store O (and LSE) ----
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (g < cnt) {
-      const int64_t t = int64_t(q0) + first + g;
-      const float inv = 1.f / l[g];
-      float o[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = acc[g][e] * inv;
-      T* ob = reinterpret_cast<T*>(a.o) + t * a.o_stride_t + int64_t(h) * a.o_stride_h + li * 8;
-      st_stream(ob, Vec8<T>::from_f32(o));
-      if (a.lse != nullptr && li == 0)
-        a.lse[t * a.lse_stride_t + int64_t(h) * a.lse_stride_h] = (m[g] + __log2f(l[g])) * kLn2;
-    }
-  }
+template <typename T, int D>
+QA_DEVINL void lds_row(const T* row, int li, uint4& lo, uint4& hi) {
+  lo = *reinterpret_cast<const uint4*>(row + li * 8);
+  hi = *reinterpret_cast<const uint4*>(row + D / 2 + li * 8);
 }
 
 template <typename T, int D>
-cudaError_t launch_d(const AncParams& p, int G, bool parents, cudaStream_t st) {
-  constexpr int LPI = D / 8;
-  const int64_t threads = p.total_items * LPI;
-  const int64_t blocks = (threads + kThreads - 1) / kThreads;
-  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  const dim3 grid{unsigned(blocks)};
-  if (parents) {
-    ancestor_attn_kernel<T, D, 1, true><<<grid, kThreads, 0, st>>>(p);
-  } else if (G == 1) {
-    ancestor_attn_kernel<T, D, 1, false><<<grid, kThreads, 0, st>>>(p);
-  } else if (G == 2) {
-    ancestor_attn_kernel<T, D, 2, false><<<grid, kThreads, 0, st>>>(p);
-  } else {
-    ancestor_attn_kernel<T, D, 4, false><<<grid, kThreads, 0, st>>>(p);
+QA_DEVINL void ldg_row(const T* row, int li, uint4& lo, uint4& hi) {
+  lo = ld_shared_row(row + li * 8);
+  hi = ld_shared_row(row + D / 2 + li * 8);
+}
+
+template <typename T>
+QA_DEVINL float dot16(const uint4& qa, const uint4& qb, const uint4& ka, const uint4& kb) {
+  float s0 = 0.f, s1 = 0.f;
+  dot_pair<T>(s0, qa.x, ka.x);
+  dot_pair<T>(s1, qa.y, ka.y);
+  dot_pair<T>(s0, qa.z, ka.z);
+  dot_pair<T>(s1, qa.w, ka.w);
+  dot_pair<T>(s0, qb.x, kb.x);
+  dot_pair<T>(s1, qb.y, kb.y);
+  dot_pair<T>(s0, qb.z, kb.z);
+  dot_pair<T>(s1, qb.w, kb.w);
+  return s0 + s1;
+}
+
+// acc += p * v over 16 elements; returns the weight actually applied.
+// fp16: p is rounded to fp16 once and applied with mixed-precision FMA (the
+// same rounded weight enters the softmax denominator, so the normalisation is
+// consistent). bf16: V is widened to fp32 (exact) and p stays fp32.
+template <typename T> struct PV;
+template <> struct PV<__half> {
+  QA_DEVINL static float apply(float (&acc)[16], float p, const uint4& va, const uint4& vb) {
+    const __half ph = __float2half_rn(p);
+    const unsigned short pb = __half_as_ushort(ph);
+    const uint32_t w[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      asm("{.reg .b16 v0, v1;\n\t"
+          "mov.b32 {v0, v1}, %2;\n\t"
+          "fma.rn.f32.f16 %0, v0, %3, %0;\n\t"
+          "fma.rn.f32.f16 %1, v1, %3, %1;}"
+          : "+f"(acc[2 * i]), "+f"(acc[2 * i + 1]) : "r"(w[i]), "h"(pb));
+    return p;  // the denominator keeps the exact weight (LSE stays fp32-accurate)
   }
+};
+template <> struct PV<__nv_bfloat16> {
+  QA_DEVINL static float apply(float (&acc)[16], float p, const uint4& va, const uint4& vb) {
+    const uint32_t w[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[2 * i] = fmaf(p, __uint_as_float(w[i] << 16), acc[2 * i]);
+      acc[2 * i + 1] = fmaf(p, __uint_as_float(w[i] & 0xffff0000u), acc[2 * i + 1]);
+    }
+    return p;
+  }
+};
+
+// Running softmax state of one query (log2 units, lazy reference maximum).
+struct SoftState {
+  float m;  // reference maximum (-inf before the first key)
+  float l;  // sum of weights relative to m
+  float acc[16];
+};
+
+template <typename T, int LPI>
+QA_DEVINL void softmax_step(SoftState& st, float s, const uint4& va, const uint4& vb) {
+  if (s > st.m + kLazy) {  // also taken for the first key (m = -inf)
+    const float alpha = fast_exp2(st.m - s);
+    st.l *= alpha;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) st.acc[e] *= alpha;
+    st.m = s;
+  }
+  st.l += PV<T>::apply(st.acc, fast_exp2(s - st.m), va, vb);
+}
+
+template <int LPI>
+QA_DEVINL float reduce_lanes(float s, unsigned mask) {
+#pragma unroll
+  for (int off = LPI / 2; off > 0; off >>= 1) s += __shfl_xor_sync(mask, s, off);
+  return s;
+}
+
+template <typename T, int D, bool PARENTS>
+__global__ void __launch_bounds__(kThreads) ancestor_attn_kernel(const AncParams p) {
+  using TL = Tile<D>;
+  constexpr int LPI = TL::LPI, MQ = TL::MQ, RC = TL::RC;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T* sQ = reinterpret_cast<T*>(smem_raw);
+  T* sK = sQ + MQ * D;
+  T* sV = sK + p.rows_cap * D;
+  __shared__ int lv_off[kMaxLevels];      // slot = lv_off[s] + node for staged level s
+  __shared__ int win_lo[kMaxLevels + 1];  // staged windows: first node, first slot
+  __shared__ int win_base[kMaxLevels + 1];
+  __shared__ int n_staged, n_win;
+
+  const qa_ancestor_args& a = p.a;
+  const int h = int(blockIdx.x % unsigned(a.num_q_heads));
+  const int rest = int(blockIdx.x / unsigned(a.num_q_heads));
+  const int tile = rest % p.tiles_per_seq;
+  const int seq = rest / p.tiles_per_seq;
+  const int q0 = __ldg(a.cu_seqlens_q + seq);
+  const int len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
+  const int q_lo = tile * MQ;
+  if (q_lo >= len) return;  // uniform over the CTA
+  const int nq = min(MQ, len - q_lo);
+  const int kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
+  const int hk = h / p.head_ratio;
+  const T* Qh = reinterpret_cast<const T*>(a.q) + int64_t(h) * a.q_stride_h;
+  const T* Kh = reinterpret_cast<const T*>(a.k) + int64_t(hk) * a.k_stride_h;
+  const T* Vh = reinterpret_cast<const T*>(a.v) + int64_t(hk) * a.v_stride_h;
+  const int tid = threadIdx.x;
+
+  // ---- plan: level ranges -> merged windows -> slot offsets (one thread) ----
+  if (tid == 0) {
+    int ns = 0, nw = 0;
+    plan_levels(q_lo, nq, PARENTS ? 0 : a.max_depth, p.div_b, p.rows_cap, lv_off, win_lo, win_base, ns, nw);
+    n_staged = ns;
+    n_win = nw;
+  }
+
+  // ---- stage the tile's Q rows ----
+  for (int c = tid; c < nq * RC; c += kThreads) {
+    const int r = c / RC, cc = c - r * RC;
+    cp_async16(sQ + r * D + cc * 8, Qh + (int64_t(q0) + q_lo + r) * a.q_stride_t + cc * 8);
+  }
+  __syncthreads();
+  // ---- stage every window's K and V rows ----
+  const int nw = n_win, nrows = win_base[nw];
+  for (int c = tid; c < nrows * RC; c += kThreads) {
+    const int j = c / RC, cc = c - j * RC;
+    int w = 0;
+    while (w + 1 < nw && win_base[w + 1] <= j) ++w;
+    const int64_t tk = int64_t(kv0) + win_lo[w] + (j - win_base[w]);
+    cp_async16(sK + j * D + cc * 8, Kh + tk * a.k_stride_t + cc * 8);
+    cp_async16(sV + j * D + cc * 8, Vh + tk * a.v_stride_t + cc * 8);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- walk: LPI lanes per query, 16 elements per lane ----
+  const int lane = tid & 31;
+  const int li = lane & (LPI - 1);
+  const unsigned mask =
+      (LPI == 32) ? 0xffffffffu : (((1u << LPI) - 1u) << (lane & ~(LPI - 1)));
+  const int nst = n_staged;
+  // next node of the walk, or -1 where the walk ends (root / self-loop / depth)
+  auto advance = [&](int node, int s) -> int {
+    if (s >= a.max_depth) return -1;
+    if constexpr (PARENTS) {
+      const int nx = __ldg(a.parents + q0 + node);
+      return (nx == node || nx < 0 || nx >= len) ? -1 : nx;
+    } else {
+      return node == 0 ? -1 : int(fast_div(uint32_t(node - 1), p.div_b));
+    }
+  };
+  for (int qi = tid / LPI; qi < nq; qi += TL::QPP) {  // uniform over a query's lanes
+    const int q = q_lo + qi;
+    const int64_t t = int64_t(q0) + q;
+    uint4 qa, qb;
+    lds_row<T, D>(sQ + qi * D, li, qa, qb);
+    SoftState st;
+    st.m = -INFINITY;
+    st.l = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) st.acc[e] = 0.f;
+    if (a.prefix_o != nullptr) {
+      // merge source: a prior result over other keys = one extra key of
+      // weight exp(prefix_lse) and value prefix_o
+      const float pl = __ldg(a.prefix_lse + t * a.prefix_lse_stride_t + int64_t(h) * a.prefix_lse_stride_h);
+      if (pl > -INFINITY) {
+        uint4 pa, pb;
+        ldg_row<T, D>(reinterpret_cast<const T*>(a.prefix_o) + t * a.prefix_o_stride_t +
+                          int64_t(h) * a.prefix_o_stride_h, li, pa, pb);
+        float f[8];
+        Vec8<T>::to_f32(pa, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) st.acc[e] = f[e];
+        Vec8<T>::to_f32(pb, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) st.acc[8 + e] = f[e];
+        st.m = pl * kLog2e;
+        st.l = 1.f;
+      }
+    }
+
+    int node = q, s = 0;
+    while (node >= 0 && s < nst) {  // staged levels: shared memory only
+      const int slot = lv_off[s] + node;
+      uint4 ka, kb, va, vb;
+      lds_row<T, D>(sK + slot * D, li, ka, kb);
+      lds_row<T, D>(sV + slot * D, li, va, vb);
+      const float sc = reduce_lanes<LPI>(dot16<T>(qa, qb, ka, kb), mask) * p.scale_log2;
+      softmax_step<T, LPI>(st, sc, va, vb);
+      node = advance(node, s);
+      ++s;
+    }
+    while (node >= 0) {  // explicit parents / levels past the staged ones
+      const int64_t tk = int64_t(kv0) + node;
+      uint4 ka, kb, va, vb;
+      ldg_row<T, D>(Kh + tk * a.k_stride_t, li, ka, kb);
+      ldg_row<T, D>(Vh + tk * a.v_stride_t, li, va, vb);
+      const float sc = reduce_lanes<LPI>(dot16<T>(qa, qb, ka, kb), mask) * p.scale_log2;
+      softmax_step<T, LPI>(st, sc, va, vb);
+      node = advance(node, s);
+      ++s;
+    }
+
+    // ---- epilogue: normalise, store O (and LSE) ----
+    const float inv = 1.f / st.l;
+    float o0[8], o1[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o0[e] = st.acc[e] * inv;
+      o1[e] = st.acc[8 + e] * inv;
+    }
+    T* ob = reinterpret_cast<T*>(a.o) + t * a.o_stride_t + int64_t(h) * a.o_stride_h;
+    st_stream(ob + li * 8, Vec8<T>::from_f32(o0));
+    st_stream(ob + D / 2 + li * 8, Vec8<T>::from_f32(o1));
+    if (a.lse != nullptr && li == 0)
+      a.lse[t * a.lse_stride_t + int64_t(h) * a.lse_stride_h] = (st.m + __log2f(st.l)) * kLn2;
+  }
+}
+
+constexpr int kMaxSmem = 200 * 1024;
+
+template <typename T, int D>
+cudaError_t launch_d(AncParams& p, bool parents, cudaStream_t st) {
+  using TL = Tile<D>;
+  const int64_t blocks = int64_t(p.a.batch) * p.tiles_per_seq * p.a.num_q_heads;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const int row_bytes = 2 * D * int(sizeof(T));  // one K row + one V row
+  const int cap_max = (kMaxSmem - TL::MQ * D * int(sizeof(T))) / row_bytes;
+  int cap = rows_needed(TL::MQ, p.a.branching, p.a.max_depth, parents);
+  p.rows_cap = cap < cap_max ? cap : cap_max;
+  const int smem = TL::MQ * D * int(sizeof(T)) + p.rows_cap * row_bytes;
+  auto kern = parents ? ancestor_attn_kernel<T, D, true> : ancestor_attn_kernel<T, D, false>;
+  static bool attr_set[2] = {false, false};  // per instance, once per process
+  if (!attr_set[parents]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[parents] = true;
+  }
+  kern<<<dim3{unsigned(blocks)}, kThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t launch_t(const AncParams& p, int G, bool parents, cudaStream_t st) {
+cudaError_t launch_t(AncParams& p, bool parents, cudaStream_t st) {
   switch (p.a.head_dim) {
-    case 32: return launch_d<T, 32>(p, G, parents, st);
-    case 64: return launch_d<T, 64>(p, G, parents, st);
-    case 128: return launch_d<T, 128>(p, G, parents, st);
-    default: return launch_d<T, 256>(p, G, parents, st);
+    case 32: return launch_d<T, 32>(p, parents, st);
+    case 64: return launch_d<T, 64>(p, parents, st);
+    case 128: return launch_d<T, 128>(p, parents, st);
+    default: return launch_d<T, 256>(p, parents, st);
   }
 }
 
@@ -322,24 +353,14 @@ extern "C" int qa_ancestor_attn(const qa_ancestor_args* args, void* stream) {
   p.a = a;
   p.scale_log2 = a.scale * kLog2e;
   p.head_ratio = a.num_q_heads / a.num_kv_heads;
+  const int mq = kOwnBytes / (2 * a.head_dim);
+  p.tiles_per_seq = (a.max_seqlen + mq - 1) / mq;
   const bool parents = a.parents != nullptr;
-  int G = 1;
-  if (parents) {
-    p.chunks = 1;
-    p.groups_per_seq = a.max_seqlen;
-  } else {
-    const int b = a.branching;
-    G = (b == 1) ? 1 : (b == 2 ? 2 : 4);
-    p.chunks = (b + G - 1) / G;
-    // group 0 = root, then `chunks` groups per parent p for p with p*b+1 < max_seqlen
-    const int64_t parents_needed = a.max_seqlen > 1 ? (int64_t(a.max_seqlen) - 2) / b + 1 : 0;
-    const int64_t gps = 1 + parents_needed * p.chunks;
-    if (gps > 0x7fffffffLL) return QA_ERR_INVALID;
-    p.groups_per_seq = int32_t(gps);
-  }
-  p.total_items = int64_t(a.batch) * p.groups_per_seq * a.num_q_heads;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = (a.dtype == QA_DTYPE_F16) ? launch_t<__half>(p, G, parents, st)
-                                            : launch_t<__nv_bfloat16>(p, G, parents, st);
+  const int tc = ancestor_tc_launch(a, st);
+  if (tc != kTcNotApplicable) return tc;
+  p.div_b = make_fast_div(uint32_t(parents ? 1 : a.branching));
+  cudaError_t e = (a.dtype == QA_DTYPE_F16) ? launch_t<__half>(p, parents, st)
+                                            : launch_t<__nv_bfloat16>(p, parents, st);
   return e == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }

@@ -1,0 +1,425 @@
+// Ancestor-walk attention, complete-tree mode, level-at-a-time on tensor cores.
+//
+// Same result as the scalar walk in ancestor_attn.cu (and as the reference's
+// _ragged_attn_sparse_kernel(_lse), src/ragged_attn.py:267-496), organised so
+// that per-query overhead disappears:
+//   * A warp owns 16 consecutive BFS queries of one (sequence, head). At walk
+//     level s their ancestors are a contiguous node range of at most 16 rows
+//     (see ancestor_plan.cuh), already staged in shared memory by the CTA.
+//   * S = Q (16 x D) . K_level^T (D x 16) with mma.sync m16n8k16 (fp32
+//     accumulate); each query row keeps the one column that is its step-s
+//     ancestor (or none when its walk has ended), so the softmax sees exactly
+//     the reference's key set.
+//   * O += P . V_level with P the one-hot row of that weight (fp16, or bf16
+//     split into hi + lo parts so the weight keeps ~16 bits), again one
+//     m16n8k16 per 8 output columns. The softmax reference maximum moves only
+//     when a score exceeds it by 2^8 (lazy rescale; exact result).
+//   * Tensor cores here only cut instruction count (the whole kernel is a
+//     gather with ~2.8 flop per HBM byte): one level of 16 queries costs ~70
+//     warp instructions instead of ~650 for a per-query scalar walk.
+//   * Shared rows use a 16-byte-chunk XOR swizzle (chunk ^ (row & 7)) so the
+//     ldmatrix row reads are bank-conflict free; the output tile is written
+//     back through the same shared region as 16-byte row vectors.
+// Used when every walk level of a tile fits in shared memory (always true for
+// b >= 2; chains up to depth ~300), for head_dim 64, 128 and 256.
+#include "ancestor_plan.cuh"
+
+namespace qa {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kTcThreads = kWarps * 32;
+constexpr int kTcMQ = kWarps * 16;  // queries per CTA
+constexpr int kTcMaxSmem = 200 * 1024;
+constexpr int kTcMaxKeys = 128;  // key-list columns per warp (all walk levels of 16 queries)
+
+struct TcParams {
+  qa_ancestor_args a;
+  float scale_log2;
+  int32_t tiles_per_seq;
+  int32_t head_ratio;
+  int32_t rows_cap;
+  int32_t kw_cap;  // key-list columns per warp (multiple of 16)
+  int32_t heads_per_cta;
+  FastDiv div_b;
+};
+
+QA_DEVINL uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+QA_DEVINL void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+QA_DEVINL void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+template <typename T> QA_DEVINL void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <> QA_DEVINL void mma16816<__half>(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <> QA_DEVINL void mma16816<__nv_bfloat16>(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two fp32 -> packed pair of T (low element first).
+template <typename T> QA_DEVINL uint32_t pack2(float lo, float hi);
+template <> QA_DEVINL uint32_t pack2<__half>(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <> QA_DEVINL uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// Byte offset of 16-byte chunk c of row r in a swizzled [rows][D] tile.
+template <int D> QA_DEVINL uint32_t swz(int r, int c) {
+  return uint32_t(r) * (D * 2) + uint32_t((c ^ (r & 7)) * 16);
+}
+
+// Dynamic shared memory of one CTA (bytes): Q tile, staged K and V rows, and
+// the token row of every staged slot.
+template <int D> struct TcSmem {
+  __host__ __device__ static int k_off() { return kTcMQ * D * 2; }
+  __host__ __device__ static int v_off(int rows) { return k_off() + rows * D * 2; }
+  __host__ __device__ static int tok_off(int rows) { return v_off(rows) + rows * D * 2; }
+  __host__ __device__ static int total(int rows) { return tok_off(rows) + rows * 4; }
+};
+
+template <typename T, int D, int NBK>
+__global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams p) {
+  using SM = TcSmem<D>;
+  constexpr int RC = D / 8;   // 16-byte chunks per row
+  constexpr int KB = D / 16;  // k16 steps of q.k
+  constexpr int NB = D / 8;   // n8 blocks of the output
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int kw = p.kw_cap;
+  unsigned char* sQ = smem_raw;
+  unsigned char* sK = smem_raw + SM::k_off();
+  unsigned char* sV = smem_raw + SM::v_off(p.rows_cap);
+  int* row_tok = reinterpret_cast<int*>(smem_raw + SM::tok_off(p.rows_cap));
+  __shared__ int lv_off[kMaxLevels];
+  __shared__ int win_lo[kMaxLevels + 1];
+  __shared__ int win_base[kMaxLevels + 1];
+  __shared__ int n_staged, n_win;
+  __shared__ int w_col[kWarps][kMaxLevels];       // column = w_col[s] + node, per warp
+  __shared__ int w_lo[kWarps][kMaxLevels + 1];    // per-warp key windows
+  __shared__ int w_base[kWarps][kMaxLevels + 1];
+  __shared__ int w_levels[kWarps], w_nwin[kWarps];
+  __shared__ int kslot[kWarps][kTcMaxKeys];       // staged K/V row of each key column
+
+  const qa_ancestor_args& a = p.a;
+  const int hgroups = (a.num_q_heads + p.heads_per_cta - 1) / p.heads_per_cta;
+  const int h_first = int(blockIdx.x % unsigned(hgroups)) * p.heads_per_cta;
+  const int h_end = min(h_first + p.heads_per_cta, a.num_q_heads);
+  const int rest = int(blockIdx.x / unsigned(hgroups));
+  const int tile = rest % p.tiles_per_seq;
+  const int seq = rest / p.tiles_per_seq;
+  const int q0 = __ldg(a.cu_seqlens_q + seq);
+  const int len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
+  const int q_lo = tile * kTcMQ;
+  if (q_lo >= len) return;  // uniform over the CTA
+  const int nq = min(kTcMQ, len - q_lo);
+  const int kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int wrow = warp * 16;  // first tile row of this warp
+  const int wn = max(0, min(16, nq - wrow));
+  const int wq_lo = q_lo + wrow;
+
+  // ---- CTA plan (levels -> staged windows), shared by every head ----
+  if (tid == 0) {
+    int ns = 0, nw = 0;
+    plan_levels(q_lo, nq, a.max_depth, p.div_b, p.rows_cap, lv_off, win_lo, win_base, ns, nw);
+    n_staged = ns;
+    n_win = nw;
+  }
+  __syncthreads();
+  const int nw = n_win, nrows = win_base[nw];
+  for (int j = tid; j < nrows; j += kTcThreads) {  // token row of every staged slot
+    int w = 0;
+    while (w + 1 < nw && win_base[w + 1] <= j) ++w;
+    row_tok[j] = kv0 + win_lo[w] + (j - win_base[w]);
+  }
+  // ---- per-warp key list: the warp's level ranges merged into windows ----
+  if (lane == 0 && wn > 0) {
+    int L = 0, nwin = 0;
+    plan_levels(wq_lo, wn, a.max_depth, p.div_b, kw, w_col[warp], w_lo[warp], w_base[warp], L, nwin);
+    w_levels[warp] = L;
+    w_nwin[warp] = nwin;
+  }
+  __syncthreads();
+  // key column -> staged slot (columns past the list repeat its last row)
+  const int nkeys = wn > 0 ? w_base[warp][w_nwin[warp]] : 0;
+  const int kpad = (nkeys + 15) & ~15;
+  if (wn > 0) {
+    const int nwin = w_nwin[warp];
+    for (int c = lane; c < kpad; c += 32) {
+      const int cc = min(c, nkeys - 1);
+      int wi = 0;
+      while (wi + 1 < nwin && w_base[warp][wi + 1] <= cc) ++wi;
+      const int node = w_lo[warp][wi] + (cc - w_base[warp][wi]);
+      int cw = 0;  // the CTA window that stages this node
+      while (cw + 1 < nw && node < win_lo[cw]) ++cw;  // windows descend in node order
+      kslot[warp][c] = win_base[cw] + node - win_lo[cw];
+    }
+  }
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t kbase = smem_u32(sK), vbase = smem_u32(sV);
+  const int* ks = kslot[warp];
+  int hk_staged = -1;
+  for (int h = h_first; h < h_end; ++h) {
+  // ---- stage this head's Q rows, and K/V rows when the KV head changes ----
+  const int hk = h / p.head_ratio;
+  const T* Qh = reinterpret_cast<const T*>(a.q) + int64_t(h) * a.q_stride_h;
+  for (int c = tid; c < nq * RC; c += kTcThreads) {
+    const int r = c / RC, cc = c - r * RC;
+    cp_async16(sQ + swz<D>(r, cc), Qh + (int64_t(q0) + q_lo + r) * a.q_stride_t + cc * 8);
+  }
+  if (hk != hk_staged) {
+    const T* Kh = reinterpret_cast<const T*>(a.k) + int64_t(hk) * a.k_stride_h;
+    const T* Vh = reinterpret_cast<const T*>(a.v) + int64_t(hk) * a.v_stride_h;
+    for (int c = tid; c < nrows * RC; c += kTcThreads) {
+      const int j = c / RC, cc = c - j * RC;
+      const int64_t tk = row_tok[j];
+      cp_async16(sK + swz<D>(j, cc), Kh + tk * a.k_stride_t + cc * 8);
+      cp_async16(sV + swz<D>(j, cc), Vh + tk * a.v_stride_t + cc * 8);
+    }
+    hk_staged = hk;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (wn > 0) {
+  // ---- S = Q . K_list^T over every level's keys at once (registers) ----
+  uint32_t qf[KB][4];
+#pragma unroll
+  for (int kk = 0; kk < KB; ++kk)
+    ldsm_x4(smem_u32(sQ) + swz<D>(wrow + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1],
+            qf[kk][2], qf[kk][3]);
+  float sc[NBK][4];
+#pragma unroll
+  for (int nb = 0; nb < NBK; ++nb) {
+    sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+    if (8 * nb < kpad) {
+      const int slot = ks[8 * nb + (lane & 7)];
+#pragma unroll
+      for (int k2 = 0; k2 < KB / 2; ++k2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + swz<D>(slot, 4 * k2 + (lane >> 3)), b0, b1, b2, b3);
+        mma16816<T>(sc[nb], qf[2 * k2], b0, b1);
+        mma16816<T>(sc[nb], qf[2 * k2 + 1], b2, b3);
+      }
+    }
+  }
+  // ---- which fragment elements are this thread's rows' walk keys ----
+  // Row r's step-s key is column w_col[s] + node_s(r); the thread owning
+  // column c of a row holds it in block c/8, element c%2 when (c%8)/2 == t.
+  uint32_t sel0 = 0u, sel1 = 0u;
+  {
+    const int L = w_levels[warp];
+    const int* wc = w_col[warp];
+    int n0 = g < wn ? wq_lo + g : -1, n1 = g + 8 < wn ? wq_lo + g + 8 : -1;
+    for (int s = 0; s < L; ++s) {
+      if (s > 0) {
+        n0 = n0 <= 0 ? -1 : int(fast_div(uint32_t(n0 - 1), p.div_b));
+        n1 = n1 <= 0 ? -1 : int(fast_div(uint32_t(n1 - 1), p.div_b));
+      }
+      const int off = wc[s];
+      const int c0 = off + n0, c1 = off + n1;
+      if (n0 >= 0 && ((c0 >> 1) & 3) == t) sel0 |= 1u << (((c0 >> 3) << 1) | (c0 & 1));
+      if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
+    }
+  }
+  // ---- exact softmax per row over its walk (a quad of threads shares a row) ----
+  float mx0 = -INFINITY, mx1 = -INFINITY, pl0 = -INFINITY, pl1 = -INFINITY;
+  if (a.prefix_o != nullptr) {
+    const int64_t t0 = int64_t(q0) + wq_lo + g;
+    if (g < wn) pl0 = __ldg(a.prefix_lse + t0 * a.prefix_lse_stride_t + int64_t(h) * a.prefix_lse_stride_h) * kLog2e;
+    if (g + 8 < wn) pl1 = __ldg(a.prefix_lse + (t0 + 8) * a.prefix_lse_stride_t + int64_t(h) * a.prefix_lse_stride_h) * kLog2e;
+    mx0 = pl0;
+    mx1 = pl1;
+  }
+#pragma unroll
+  for (int nb = 0; nb < NBK; ++nb)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sc[nb][e] *= p.scale_log2;
+      sc[nb][2 + e] *= p.scale_log2;
+      if ((sel0 >> (2 * nb + e)) & 1u) mx0 = fmaxf(mx0, sc[nb][e]);
+      if ((sel1 >> (2 * nb + e)) & 1u) mx1 = fmaxf(mx1, sc[nb][2 + e]);
+    }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+  for (int nb = 0; nb < NBK; ++nb)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sc[nb][e] = ((sel0 >> (2 * nb + e)) & 1u) ? fast_exp2(sc[nb][e] - mx0) : 0.f;
+      sc[nb][2 + e] = ((sel1 >> (2 * nb + e)) & 1u) ? fast_exp2(sc[nb][2 + e] - mx1) : 0.f;
+      l0 += sc[nb][e];
+      l1 += sc[nb][2 + e];
+    }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float wp0 = pl0 > -INFINITY ? fast_exp2(pl0 - mx0) : 0.f;  // prefix weights
+  const float wp1 = pl1 > -INFINITY ? fast_exp2(pl1 - mx1) : 0.f;
+  l0 += wp0;
+  l1 += wp1;
+  if (a.lse != nullptr && t == 0) {
+    float* Lh = a.lse + int64_t(h) * a.lse_stride_h;
+    if (g < wn) Lh[(int64_t(q0) + wq_lo + g) * a.lse_stride_t] = (mx0 + __log2f(l0)) * kLn2;
+    if (g + 8 < wn) Lh[(int64_t(q0) + wq_lo + g + 8) * a.lse_stride_t] = (mx1 + __log2f(l1)) * kLn2;
+  }
+  const float inv0 = g < wn ? 1.f / l0 : 0.f;
+  const float inv1 = g + 8 < wn ? 1.f / l1 : 0.f;
+
+  // ---- O = prefix weight * prefix_o + P . V_list (P from the S registers) ----
+  float o[NB][4];
+#pragma unroll
+  for (int j = 0; j < NB; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  if (a.prefix_o != nullptr) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = g + 8 * half;
+      const float wgt = half ? wp1 : wp0;
+      if (r >= wn || wgt == 0.f) continue;
+      const int64_t tq = int64_t(q0) + wq_lo + r;
+      const T* po = reinterpret_cast<const T*>(a.prefix_o) + tq * a.prefix_o_stride_t + int64_t(h) * a.prefix_o_stride_h;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const float2 f = pair_to_f32<T>(__ldg(reinterpret_cast<const unsigned int*>(po + 8 * j + 2 * t)));
+        o[j][2 * half] = wgt * f.x;
+        o[j][2 * half + 1] = wgt * f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int kp = 0; kp < NBK / 2; ++kp) {
+    if (16 * kp >= kpad) break;
+    uint32_t pa[4];
+    pa[0] = pack2<T>(sc[2 * kp][0], sc[2 * kp][1]);
+    pa[1] = pack2<T>(sc[2 * kp][2], sc[2 * kp][3]);
+    pa[2] = pack2<T>(sc[2 * kp + 1][0], sc[2 * kp + 1][1]);
+    pa[3] = pack2<T>(sc[2 * kp + 1][2], sc[2 * kp + 1][3]);
+    uint32_t pb[4] = {0u, 0u, 0u, 0u};
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      // bf16 keeps 8 mantissa bits: the rounding remainder goes in a second product
+      auto rem = [](float x) { return x - __bfloat162float(__float2bfloat16_rn(x)); };
+      pb[0] = pack2<T>(rem(sc[2 * kp][0]), rem(sc[2 * kp][1]));
+      pb[1] = pack2<T>(rem(sc[2 * kp][2]), rem(sc[2 * kp][3]));
+      pb[2] = pack2<T>(rem(sc[2 * kp + 1][0]), rem(sc[2 * kp + 1][1]));
+      pb[3] = pack2<T>(rem(sc[2 * kp + 1][2]), rem(sc[2 * kp + 1][3]));
+    }
+    const int slot = ks[16 * kp + (lane & 7) + 8 * ((lane >> 3) & 1)];
+#pragma unroll
+    for (int jp = 0; jp < D / 16; ++jp) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vbase + swz<D>(slot, 2 * jp + (lane >> 4)), b0, b1, b2, b3);
+      mma16816<T>(o[2 * jp], pa, b0, b1);
+      mma16816<T>(o[2 * jp + 1], pa, b2, b3);
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        mma16816<T>(o[2 * jp], pb, b0, b1);
+        mma16816<T>(o[2 * jp + 1], pb, b2, b3);
+      }
+    }
+  }
+
+  // ---- epilogue: normalise, stage the tile in this warp's Q rows, store ----
+#pragma unroll
+  for (int j = 0; j < NB; ++j) {
+    *reinterpret_cast<uint32_t*>(sQ + swz<D>(wrow + g, j) + 4 * t) = pack2<T>(o[j][0] * inv0, o[j][1] * inv0);
+    *reinterpret_cast<uint32_t*>(sQ + swz<D>(wrow + g + 8, j) + 4 * t) = pack2<T>(o[j][2] * inv1, o[j][3] * inv1);
+  }
+  __syncwarp();
+  T* Oh = reinterpret_cast<T*>(a.o) + int64_t(h) * a.o_stride_h;
+  for (int i = lane; i < wn * RC; i += 32) {
+    const int r = i / RC, c = i - r * RC;
+    const uint4 v = *reinterpret_cast<const uint4*>(sQ + swz<D>(wrow + r, c));
+    st_stream(Oh + (int64_t(q0) + wq_lo + r) * a.o_stride_t + c * 8, v);
+  }
+  }  // wn > 0
+  __syncthreads();  // shared tiles are overwritten by the next head
+  }  // heads
+}
+
+template <typename T, int D, int NBK>
+int launch_tc(TcParams& p, cudaStream_t st) {
+  const int64_t blocks = int64_t(p.a.batch) * p.tiles_per_seq *
+                        ((p.a.num_q_heads + p.heads_per_cta - 1) / p.heads_per_cta);
+  if (blocks > 0x7fffffffLL) return QA_ERR_INVALID;
+  const int smem = TcSmem<D>::total(p.rows_cap);
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(ancestor_tc_kernel<T, D, NBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kTcMaxSmem) != cudaSuccess)
+      return QA_ERR_LAUNCH;
+    attr_set = true;
+  }
+  ancestor_tc_kernel<T, D, NBK><<<dim3{unsigned(blocks)}, kTcThreads, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
+}
+
+template <typename T, int D>
+int launch_tc_nbk(TcParams& p, cudaStream_t st) {
+  if (p.kw_cap <= 32) return launch_tc<T, D, 4>(p, st);
+  if (p.kw_cap <= 64) return launch_tc<T, D, 8>(p, st);
+  return launch_tc<T, D, 16>(p, st);
+}
+
+}  // namespace
+
+// Launches the tensor-core level kernel when it applies (complete-tree mode,
+// head_dim 64/128/256, every level of a tile fits in shared memory); returns
+// kTcNotApplicable otherwise so the caller runs the scalar walk. Arguments are
+// already validated by qa_ancestor_attn.
+int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
+  if (a.parents != nullptr) return kTcNotApplicable;
+  if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return kTcNotApplicable;
+  if (a.branching == 1 && a.max_depth >= kMaxLevels) return kTcNotApplicable;
+  const int rows = rows_needed(kTcMQ, a.branching, a.max_depth, false);
+  const int kw = (rows_needed(16, a.branching, a.max_depth, false) + 15) & ~15;
+  if (kw > kTcMaxKeys) return kTcNotApplicable;
+  const int smem = a.head_dim == 64 ? TcSmem<64>::total(rows)
+                 : a.head_dim == 128 ? TcSmem<128>::total(rows) : TcSmem<256>::total(rows);
+  if (smem > kTcMaxSmem) return kTcNotApplicable;
+  TcParams p;
+  p.a = a;
+  p.scale_log2 = a.scale * kLog2e;
+  p.tiles_per_seq = (a.max_seqlen + kTcMQ - 1) / kTcMQ;
+  p.head_ratio = a.num_q_heads / a.num_kv_heads;
+  p.rows_cap = rows;
+  p.kw_cap = kw;
+  // heads per CTA: amortise the plan while keeping >= ~4 CTAs per SM of work
+  {
+    const int64_t tiles = int64_t(a.batch) * p.tiles_per_seq;
+    int hpc = 1;
+    while (hpc * 2 <= a.num_q_heads && tiles * ((a.num_q_heads + 2 * hpc - 1) / (2 * hpc)) >= 4 * 148) hpc *= 2;
+    if (a.num_q_heads % p.head_ratio == 0 && hpc < p.head_ratio && p.head_ratio <= a.num_q_heads) hpc = p.head_ratio;
+    p.heads_per_cta = hpc;
+  }
+  p.div_b = make_fast_div(uint32_t(a.branching));
+  const bool bf = a.dtype == QA_DTYPE_BF16;
+  switch (a.head_dim) {
+    case 64: return bf ? launch_tc_nbk<__nv_bfloat16, 64>(p, st) : launch_tc_nbk<__half, 64>(p, st);
+    case 128: return bf ? launch_tc_nbk<__nv_bfloat16, 128>(p, st) : launch_tc_nbk<__half, 128>(p, st);
+    default: return bf ? launch_tc_nbk<__nv_bfloat16, 256>(p, st) : launch_tc_nbk<__half, 256>(p, st);
+  }
+}
+
+}  // namespace qa

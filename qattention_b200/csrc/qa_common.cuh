@@ -86,6 +86,53 @@ QA_DEVINL void st_stream(void* p, const uint4& v) {
                : "memory");
 }
 
+// acc += a.lo*b.lo + a.hi*b.hi for packed pairs of 16-bit elements, products
+// and sums in fp32 (sm_100 mixed-precision FMA, no conversion instructions).
+template <typename T> QA_DEVINL void dot_pair(float& acc, uint32_t a, uint32_t b);
+template <> QA_DEVINL void dot_pair<__half>(float& acc, uint32_t a, uint32_t b) {
+  asm("{.reg .b16 a0, a1, b0, b1;\n\t"
+      "mov.b32 {a0, a1}, %1;\n\t"
+      "mov.b32 {b0, b1}, %2;\n\t"
+      "fma.rn.f32.f16 %0, a0, b0, %0;\n\t"
+      "fma.rn.f32.f16 %0, a1, b1, %0;}"
+      : "+f"(acc) : "r"(a), "r"(b));
+}
+template <> QA_DEVINL void dot_pair<__nv_bfloat16>(float& acc, uint32_t a, uint32_t b) {
+  asm("{.reg .b16 a0, a1, b0, b1;\n\t"
+      "mov.b32 {a0, a1}, %1;\n\t"
+      "mov.b32 {b0, b1}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, a0, b0, %0;\n\t"
+      "fma.rn.f32.bf16 %0, a1, b1, %0;}"
+      : "+f"(acc) : "r"(a), "r"(b));
+}
+
+// Packed pair of 16-bit elements -> two fp32 (exact).
+template <typename T> QA_DEVINL float2 pair_to_f32(uint32_t w);
+template <> QA_DEVINL float2 pair_to_f32<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <> QA_DEVINL float2 pair_to_f32<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// 16-byte asynchronous global->shared copy that bypasses L1 (cp.async.cg).
+QA_DEVINL void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+QA_DEVINL void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// x / d for 0 <= x < 2^31 with a precomputed multiplier (round-up method of
+// Granlund & Montgomery, 1994): l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1,
+// x / d = (umulhi(x, m) + x) >> l.
+struct FastDiv {
+  uint32_t m;
+  uint32_t l;
+};
+QA_DEVINL uint32_t fast_div(uint32_t x, FastDiv f) { return (__umulhi(x, f.m) + x) >> f.l; }
+
 QA_DEVINL float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
