@@ -65,6 +65,39 @@ QA_DEVINL void plan_levels(int q_lo, int nq, int max_depth, FastDiv div_b, int r
   n_windows = nw;
 }
 
+// Single-pass form of plan_levels for callers that know every level fits
+// (no capacity check, no local arrays): ranges only move towards the root, so
+// each new range either extends the open window downwards or closes it.
+QA_DEVINL void plan_levels_fit(int q_lo, int nq, int max_depth, FastDiv div_b, int* lv_off,
+                               int* win_lo, int* win_base, int& n_levels, int& n_windows) {
+  int lo = q_lo, hi = q_lo + nq - 1;
+  int wlo = lo, whi = hi, nw = 0, cum = 0, L = 1;
+  lv_off[0] = 0;  // provisional window index, turned into an offset below
+  while (L < kMaxLevels && L <= max_depth && hi > 0) {
+    lo = int(fast_div(uint32_t(max(lo, 1) - 1), div_b));
+    hi = int(fast_div(uint32_t(hi - 1), div_b));
+    if (hi >= wlo - 1) {
+      wlo = min(wlo, lo);
+    } else {
+      win_lo[nw] = wlo;
+      win_base[nw] = cum;
+      cum += whi - wlo + 1;
+      ++nw;
+      wlo = lo;
+      whi = hi;
+    }
+    lv_off[L++] = nw;
+  }
+  win_lo[nw] = wlo;
+  win_base[nw] = cum;
+  cum += whi - wlo + 1;
+  ++nw;
+  win_base[nw] = cum;
+  for (int s = 0; s < L; ++s) lv_off[s] = win_base[lv_off[s]] - win_lo[lv_off[s]];
+  n_levels = L;
+  n_windows = nw;
+}
+
 // Upper bound on the K/V rows plan_levels needs for a tile of mq queries.
 // If level s-1 spans nodes [lo, lo + span], its parents span at most
 // floor(span / b) + 1 nodes more than one, so span_s <= span_{s-1} / b + 1 and

@@ -89,12 +89,12 @@ template <int D> QA_DEVINL uint32_t swz(int r, int c) {
 }
 
 // Dynamic shared memory of one CTA (bytes): Q tile, staged K and V rows, and
-// the token row of every staged slot.
+// the K and V element offsets of every staged row.
 template <int D> struct TcSmem {
   __host__ __device__ static int k_off() { return kTcMQ * D * 2; }
   __host__ __device__ static int v_off(int rows) { return k_off() + rows * D * 2; }
   __host__ __device__ static int tok_off(int rows) { return v_off(rows) + rows * D * 2; }
-  __host__ __device__ static int total(int rows) { return tok_off(rows) + rows * 4; }
+  __host__ __device__ static int total(int rows) { return tok_off(rows) + rows * 16; }
 };
 
 template <typename T, int D, int NBK>
@@ -104,11 +104,10 @@ __global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams 
   constexpr int KB = D / 16;  // k16 steps of q.k
   constexpr int NB = D / 8;   // n8 blocks of the output
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  const int kw = p.kw_cap;
   unsigned char* sQ = smem_raw;
   unsigned char* sK = smem_raw + SM::k_off();
   unsigned char* sV = smem_raw + SM::v_off(p.rows_cap);
-  int* row_tok = reinterpret_cast<int*>(smem_raw + SM::tok_off(p.rows_cap));
+  int64_t* row_off = reinterpret_cast<int64_t*>(smem_raw + SM::tok_off(p.rows_cap));
   __shared__ int lv_off[kMaxLevels];
   __shared__ int win_lo[kMaxLevels + 1];
   __shared__ int win_base[kMaxLevels + 1];
@@ -141,21 +140,23 @@ __global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams 
   // ---- CTA plan (levels -> staged windows), shared by every head ----
   if (tid == 0) {
     int ns = 0, nw = 0;
-    plan_levels(q_lo, nq, a.max_depth, p.div_b, p.rows_cap, lv_off, win_lo, win_base, ns, nw);
+    plan_levels_fit(q_lo, nq, a.max_depth, p.div_b, lv_off, win_lo, win_base, ns, nw);
     n_staged = ns;
     n_win = nw;
   }
   __syncthreads();
   const int nw = n_win, nrows = win_base[nw];
-  for (int j = tid; j < nrows; j += kTcThreads) {  // token row of every staged slot
+  for (int j = tid; j < nrows; j += kTcThreads) {  // element offset of every staged row
     int w = 0;
     while (w + 1 < nw && win_base[w + 1] <= j) ++w;
-    row_tok[j] = kv0 + win_lo[w] + (j - win_base[w]);
+    const int64_t tk = int64_t(kv0) + win_lo[w] + (j - win_base[w]);
+    row_off[2 * j] = tk * a.k_stride_t;
+    row_off[2 * j + 1] = tk * a.v_stride_t;
   }
   // ---- per-warp key list: the warp's level ranges merged into windows ----
   if (lane == 0 && wn > 0) {
     int L = 0, nwin = 0;
-    plan_levels(wq_lo, wn, a.max_depth, p.div_b, kw, w_col[warp], w_lo[warp], w_base[warp], L, nwin);
+    plan_levels_fit(wq_lo, wn, a.max_depth, p.div_b, w_col[warp], w_lo[warp], w_base[warp], L, nwin);
     w_levels[warp] = L;
     w_nwin[warp] = nwin;
   }
@@ -178,23 +179,45 @@ __global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams 
   const int g = lane >> 2, t = lane & 3;
   const uint32_t kbase = smem_u32(sK), vbase = smem_u32(sV);
   const int* ks = kslot[warp];
+  // ---- which fragment elements are this thread's rows' walk keys ----
+  // Row r's step-s key is column w_col[s] + node_s(r); the thread owning
+  // column c of a row holds it in block c/8, element c%2 when (c%8)/2 == t.
+  uint32_t sel0 = 0u, sel1 = 0u;  // same for every head
+  if (wn > 0) {
+    const int L = w_levels[warp];
+    const int* wc = w_col[warp];
+    int n0 = g < wn ? wq_lo + g : -1, n1 = g + 8 < wn ? wq_lo + g + 8 : -1;
+    for (int s = 0; s < L; ++s) {
+      if (s > 0) {
+        n0 = n0 <= 0 ? -1 : int(fast_div(uint32_t(n0 - 1), p.div_b));
+        n1 = n1 <= 0 ? -1 : int(fast_div(uint32_t(n1 - 1), p.div_b));
+      }
+      const int off = wc[s];
+      const int c0 = off + n0, c1 = off + n1;
+      if (n0 >= 0 && ((c0 >> 1) & 3) == t) sel0 |= 1u << (((c0 >> 3) << 1) | (c0 & 1));
+      if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
+    }
+  }
   int hk_staged = -1;
+  constexpr int RPP = kTcThreads / RC;
+  const int my_cc = tid % RC, my_r0 = tid / RC;
   for (int h = h_first; h < h_end; ++h) {
   // ---- stage this head's Q rows, and K/V rows when the KV head changes ----
+  // (each thread always copies the same 16-byte chunk column, RPP rows apart)
   const int hk = h / p.head_ratio;
-  const T* Qh = reinterpret_cast<const T*>(a.q) + int64_t(h) * a.q_stride_h;
-  for (int c = tid; c < nq * RC; c += kTcThreads) {
-    const int r = c / RC, cc = c - r * RC;
-    cp_async16(sQ + swz<D>(r, cc), Qh + (int64_t(q0) + q_lo + r) * a.q_stride_t + cc * 8);
+  {
+    const T* src = reinterpret_cast<const T*>(a.q) + int64_t(h) * a.q_stride_h +
+                   (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8;
+    const int64_t step = int64_t(RPP) * a.q_stride_t;
+    for (int r = my_r0; r < nq; r += RPP, src += step) cp_async16(sQ + swz<D>(r, my_cc), src);
   }
   if (hk != hk_staged) {
-    const T* Kh = reinterpret_cast<const T*>(a.k) + int64_t(hk) * a.k_stride_h;
-    const T* Vh = reinterpret_cast<const T*>(a.v) + int64_t(hk) * a.v_stride_h;
-    for (int c = tid; c < nrows * RC; c += kTcThreads) {
-      const int j = c / RC, cc = c - j * RC;
-      const int64_t tk = row_tok[j];
-      cp_async16(sK + swz<D>(j, cc), Kh + tk * a.k_stride_t + cc * 8);
-      cp_async16(sV + swz<D>(j, cc), Vh + tk * a.v_stride_t + cc * 8);
+    const T* Kh = reinterpret_cast<const T*>(a.k) + int64_t(hk) * a.k_stride_h + my_cc * 8;
+    const T* Vh = reinterpret_cast<const T*>(a.v) + int64_t(hk) * a.v_stride_h + my_cc * 8;
+    for (int j = my_r0; j < nrows; j += RPP) {
+      const uint32_t d = swz<D>(j, my_cc);
+      cp_async16(sK + d, Kh + row_off[2 * j]);
+      cp_async16(sV + d, Vh + row_off[2 * j + 1]);
     }
     hk_staged = hk;
   }
@@ -208,37 +231,22 @@ __global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams 
     ldsm_x4(smem_u32(sQ) + swz<D>(wrow + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1],
             qf[kk][2], qf[kk][3]);
   float sc[NBK][4];
+  int kslot_nb[NBK];
 #pragma unroll
   for (int nb = 0; nb < NBK; ++nb) {
     sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
-    if (8 * nb < kpad) {
-      const int slot = ks[8 * nb + (lane & 7)];
+    kslot_nb[nb] = 8 * nb < kpad ? ks[8 * nb + (lane & 7)] : 0;
+  }
 #pragma unroll
-      for (int k2 = 0; k2 < KB / 2; ++k2) {
+  for (int k2 = 0; k2 < KB / 2; ++k2) {  // k outer: NBK independent accumulation chains
+#pragma unroll
+    for (int nb = 0; nb < NBK; ++nb) {
+      if (8 * nb < kpad) {
         uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + swz<D>(slot, 4 * k2 + (lane >> 3)), b0, b1, b2, b3);
+        ldsm_x4(kbase + swz<D>(kslot_nb[nb], 4 * k2 + (lane >> 3)), b0, b1, b2, b3);
         mma16816<T>(sc[nb], qf[2 * k2], b0, b1);
         mma16816<T>(sc[nb], qf[2 * k2 + 1], b2, b3);
       }
-    }
-  }
-  // ---- which fragment elements are this thread's rows' walk keys ----
-  // Row r's step-s key is column w_col[s] + node_s(r); the thread owning
-  // column c of a row holds it in block c/8, element c%2 when (c%8)/2 == t.
-  uint32_t sel0 = 0u, sel1 = 0u;
-  {
-    const int L = w_levels[warp];
-    const int* wc = w_col[warp];
-    int n0 = g < wn ? wq_lo + g : -1, n1 = g + 8 < wn ? wq_lo + g + 8 : -1;
-    for (int s = 0; s < L; ++s) {
-      if (s > 0) {
-        n0 = n0 <= 0 ? -1 : int(fast_div(uint32_t(n0 - 1), p.div_b));
-        n1 = n1 <= 0 ? -1 : int(fast_div(uint32_t(n1 - 1), p.div_b));
-      }
-      const int off = wc[s];
-      const int c0 = off + n0, c1 = off + n1;
-      if (n0 >= 0 && ((c0 >> 1) & 3) == t) sel0 |= 1u << (((c0 >> 3) << 1) | (c0 & 1));
-      if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
     }
   }
   // ---- exact softmax per row over its walk (a quad of threads shares a row) ----
@@ -405,12 +413,12 @@ int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
   p.head_ratio = a.num_q_heads / a.num_kv_heads;
   p.rows_cap = rows;
   p.kw_cap = kw;
-  // heads per CTA: amortise the plan while keeping >= ~4 CTAs per SM of work
+  // heads per CTA: the largest power of two that still leaves >= 2 CTAs per
+  // SM (the tile plan is computed once per CTA and reused for its heads)
   {
     const int64_t tiles = int64_t(a.batch) * p.tiles_per_seq;
     int hpc = 1;
-    while (hpc * 2 <= a.num_q_heads && tiles * ((a.num_q_heads + 2 * hpc - 1) / (2 * hpc)) >= 4 * 148) hpc *= 2;
-    if (a.num_q_heads % p.head_ratio == 0 && hpc < p.head_ratio && p.head_ratio <= a.num_q_heads) hpc = p.head_ratio;
+    while (hpc * 2 <= a.num_q_heads && tiles * ((a.num_q_heads + 2 * hpc - 1) / (2 * hpc)) >= 2 * 148) hpc *= 2;
     p.heads_per_cta = hpc;
   }
   p.div_b = make_fast_div(uint32_t(a.branching));
