@@ -345,7 +345,7 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
                      "frac": per_gpu_gbs / peak, "peak_kind": peak_kind,
                      "traffic": traffic, "algorithmic_bytes": nbytes,
-                     "kernel": "ancestor_attn_kernel (qa_ancestor_attn)"},
+                     "kernel": "ancestor_tc_kernel (qa_ancestor_attn)"},
         "cpu_baseline": cpu_base,
         "e2e": {"value": nbytes * ws / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": in_bytes,
