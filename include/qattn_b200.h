@@ -113,6 +113,52 @@ QA_API int qa_lse_merge(const float* lse_a, const float* lse_b, const void* out_
                  const int64_t* out_b_strides /*[3]*/,
                  const int64_t* out_strides /*[3]*/, int32_t dtype, void* stream);
 
+/*
+ * Shared-prefix pass: attention of each sequence's N tree queries over its L
+ * prefix keys (all prefix keys visible to every query), on tcgen05 tensor
+ * cores. Replaces the dense part of tree verification: aten flash SDPA after
+ * repeat_kv in scripts/w4a16_e2e.py:1236-1253 / :1446-1447, and the tl.dot
+ * prefix loop of _ragged_attn_hybrid_kernel (src/ragged_attn.py:1761-1800).
+ *
+ * Tensors are [batch, tokens, heads, head_dim] with element strides for the
+ * batch, token and head dimensions (head_dim stride 1; strides multiples of 8
+ * elements; 16-byte aligned bases). GQA: query head h uses KV head
+ * h / (num_q_heads / num_kv_heads); the group size must divide 128.
+ * Writes O (same dtype) and the natural-log LSE (fp32, optional). The result
+ * merges with the ancestor pass through qa_ancestor_args.prefix_o/prefix_lse.
+ * head_dim 64 or 128; prefix_len >= 1.
+ */
+typedef struct qa_prefix_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse; /* optional */
+  int64_t q_stride_b, q_stride_t, q_stride_h;
+  int64_t k_stride_b, k_stride_t, k_stride_h;
+  int64_t v_stride_b, v_stride_t, v_stride_h;
+  int64_t o_stride_b, o_stride_t, o_stride_h;
+  int64_t lse_stride_b, lse_stride_t, lse_stride_h;
+  int32_t batch;
+  int32_t num_queries; /* N: tree queries per sequence */
+  int32_t prefix_len;  /* L: prefix keys per sequence */
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  float scale;
+  int32_t dtype;
+} qa_prefix_args;
+
+QA_API int qa_prefix_attn(const qa_prefix_args* args, void* stream);
+
+/*
+ * Reads and clears the device error flag that the tensor-core kernels set when
+ * one of their bounded pipeline waits times out (a kernel that hits it stops,
+ * frees its resources and leaves its outputs incomplete). Synchronising call.
+ * *flag = 0 means no kernel has reported an error since the last call.
+ */
+QA_API int qa_check_device_error(int* flag);
+
 /* Human-readable name of a status code (static storage). */
 QA_API const char* qa_status_string(int status);
 

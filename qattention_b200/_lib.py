@@ -20,6 +20,8 @@ QA_DTYPE_BF16 = 1
 EXPORTED = (
     "qa_ancestor_attn",
     "qa_lse_merge",
+    "qa_prefix_attn",
+    "qa_check_device_error",
     "qa_status_string",
     "qa_version",
 )
@@ -47,6 +49,22 @@ class AncestorArgs(Structure):
     ]
 
 
+class PrefixArgs(Structure):
+    """Mirror of ``qa_prefix_args``."""
+
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("o", c_void_p), ("lse", c_void_p),
+        ("q_stride_b", c_int64), ("q_stride_t", c_int64), ("q_stride_h", c_int64),
+        ("k_stride_b", c_int64), ("k_stride_t", c_int64), ("k_stride_h", c_int64),
+        ("v_stride_b", c_int64), ("v_stride_t", c_int64), ("v_stride_h", c_int64),
+        ("o_stride_b", c_int64), ("o_stride_t", c_int64), ("o_stride_h", c_int64),
+        ("lse_stride_b", c_int64), ("lse_stride_t", c_int64), ("lse_stride_h", c_int64),
+        ("batch", c_int32), ("num_queries", c_int32), ("prefix_len", c_int32),
+        ("num_q_heads", c_int32), ("num_kv_heads", c_int32), ("head_dim", c_int32),
+        ("scale", c_float), ("dtype", c_int32),
+    ]
+
+
 _LIB = None
 
 
@@ -69,12 +87,23 @@ def lib() -> ctypes.CDLL:
                                    c_int32, c_int32, c_int32, c_int32,
                                    i64p, i64p, i64p, i64p, i64p, c_int32, c_void_p]
         L.qa_lse_merge.restype = c_int
+        L.qa_prefix_attn.argtypes = [POINTER(PrefixArgs), c_void_p]
+        L.qa_prefix_attn.restype = c_int
+        L.qa_check_device_error.argtypes = [POINTER(c_int)]
+        L.qa_check_device_error.restype = c_int
         L.qa_status_string.argtypes = [c_int]
         L.qa_status_string.restype = c_char_p
         L.qa_version.argtypes = []
         L.qa_version.restype = c_char_p
         _LIB = L
     return _LIB
+
+
+def device_error() -> int:
+    """Read and clear the device error flag of the pipelined kernels (synchronising)."""
+    flag = c_int(0)
+    check(lib().qa_check_device_error(ctypes.byref(flag)), "qa_check_device_error")
+    return flag.value
 
 
 def check(status: int, what: str) -> None:

@@ -249,3 +249,149 @@ def fused_lse_merge(
                         _stream_ptr(res.device))
     _lib.check(st, "qa_lse_merge")
     return res
+
+
+def prefix_attention_with_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float = None):
+    """Dense attention of tree queries over a shared KV prefix (tensor cores).
+
+    Q: ``[B, N, Hq, D]``; K, V: ``[B, L, Hkv, D]`` (any batch/token/head strides
+    with unit stride along D). Every prefix key is visible to every query; GQA
+    query head h reads KV head ``h // (Hq // Hkv)``. Returns ``O`` like Q
+    (contiguous) and ``LSE`` fp32 ``[B, N, Hq]`` in natural-log units. This is
+    the prefix phase of the reference's ``_ragged_tree_attn``
+    (scripts/w4a16_e2e.py:1236-1253), without materialising ``repeat_kv``.
+    """
+    _check_qkv(Q.flatten(0, 1), K.flatten(0, 1), V.flatten(0, 1))
+    B, N, Hq, D = Q.shape
+    L, Hkv = K.shape[1], K.shape[2]
+    O = torch.empty(B, N, Hq, D, dtype=Q.dtype, device=Q.device)
+    LSE = torch.empty(B, N, Hq, dtype=torch.float32, device=Q.device)
+    if B == 0 or N == 0:
+        return O, LSE
+    if L == 0:
+        O.zero_()
+        LSE.fill_(-math.inf)
+        return O, LSE
+    def fix(t):
+        ok = (t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:3]) and t.data_ptr() % 16 == 0)
+        return t if ok else t.contiguous()
+    Q, K, V = fix(Q), fix(K), fix(V)
+    a = _lib.PrefixArgs()
+    a.q, a.k, a.v, a.o, a.lse = Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), LSE.data_ptr()
+    a.q_stride_b, a.q_stride_t, a.q_stride_h = Q.stride(0), Q.stride(1), Q.stride(2)
+    a.k_stride_b, a.k_stride_t, a.k_stride_h = K.stride(0), K.stride(1), K.stride(2)
+    a.v_stride_b, a.v_stride_t, a.v_stride_h = V.stride(0), V.stride(1), V.stride(2)
+    a.o_stride_b, a.o_stride_t, a.o_stride_h = O.stride(0), O.stride(1), O.stride(2)
+    a.lse_stride_b, a.lse_stride_t, a.lse_stride_h = LSE.stride(0), LSE.stride(1), LSE.stride(2)
+    a.batch, a.num_queries, a.prefix_len = B, N, L
+    a.num_q_heads, a.num_kv_heads, a.head_dim = Hq, Hkv, D
+    a.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    a.dtype = _dtype_code(Q.dtype)
+    _lib.check(_lib.lib().qa_prefix_attn(a, _stream_ptr(Q.device)), "qa_prefix_attn")
+    return O, LSE
+
+
+def ragged_attention_hybrid(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    prefix_length: int,
+    tree_size: int,
+    branching_factor: int,
+    max_depth: int,
+) -> torch.Tensor:
+    """Prefix + tree attention in the reference's hybrid layout.
+
+    Q: ``[B*N, H, D]``; K, V: ``[B*(L+N), H(kv), D]`` with each sequence's L
+    prefix rows first, then its N tree rows (src/ragged_attn.py:1851-1888).
+    Every query sees all L prefix keys plus its tree ancestors. Runs the
+    tensor-core prefix pass, then the ancestor pass with the log-sum-exp merge
+    fused into it.
+    """
+    _check_qkv(Q, K, V)
+    total, H, D = Q.shape
+    N, L = int(tree_size), int(prefix_length)
+    B = total // N
+    Hkv = K.shape[1]
+    cu_q = torch.arange(0, (B + 1) * N, N, dtype=torch.int32, device=Q.device)
+    cu_kv = torch.arange(0, (B + 1) * (L + N), L + N, dtype=torch.int32, device=Q.device)
+    if L == 0:
+        O, _ = _ancestor(Q, K, V, cu_q, N, branching=branching_factor, max_depth=max_depth,
+                         cu_kv=cu_kv, kv_offset=0)
+        return O
+    Kb = K.view(B, L + N, Hkv, D)[:, :L]
+    Vb = V.view(B, L + N, Hkv, D)[:, :L]
+    Op, Lp = prefix_attention_with_lse(Q.view(B, N, H, D), Kb, Vb)
+    O, _ = _ancestor(Q, K, V, cu_q, N, branching=branching_factor, max_depth=max_depth,
+                     cu_kv=cu_kv, kv_offset=L, prefix_o=Op.view(B * N, H, D),
+                     prefix_lse=Lp.view(B * N, H), out=Op.view(B * N, H, D))
+    return O
+
+
+def tree_verify_attention(
+    Q: torch.Tensor,
+    K: torch.Tensor,
+    V: torch.Tensor,
+    branching_factor: int,
+    max_depth: int,
+    tree_parents: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Verify-step attention in the E2E caller's layout (``_ragged_tree_attn``,
+    scripts/w4a16_e2e.py:1201-1309).
+
+    Q: ``[B, Hq, N, D]`` (post-RoPE tree queries); K, V: ``[B, Hkv, L+N, D]``
+    (prefix then tree). Tree queries see every prefix key and their tree
+    ancestors (complete b-ary BFS tree, or ``tree_parents`` ``[N]`` int32 with
+    root self-loop, shared by the batch). Returns ``[B, Hq, N, D]`` (a permuted
+    view of a ``[B, N, Hq, D]`` buffer). GQA without ``repeat_kv``; no layout
+    copies of Q/K/V (the kernels take the strides).
+    """
+    B, Hq, N, D = Q.shape
+    Hkv, LN = K.shape[1], K.shape[2]
+    L = LN - N
+    Qt = Q.permute(0, 2, 1, 3)                              # [B, N, Hq, D] view
+    Kt, Vt = K.permute(0, 2, 1, 3), V.permute(0, 2, 1, 3)  # [B, L+N, Hkv, D] views
+    if L > 0:
+        out, lse = prefix_attention_with_lse(Qt, Kt[:, :L], Vt[:, :L])
+    else:
+        out = torch.empty(B, N, Hq, D, dtype=Q.dtype, device=Q.device)
+        lse = None
+    par = None
+    if tree_parents is not None:
+        par = tree_parents.to(device=Q.device, dtype=torch.int32).repeat(B).contiguous()
+    # Query rows need one token stride across the batch: copy Q once unless it already has it.
+    Qr = (Qt if Qt.is_contiguous() else Qt.contiguous()).view(B * N, Hq, D)
+    Kr, Vr, kv_rows, kv_off = _tree_rows(Kt, Vt, L, N)
+    cu_q = torch.arange(0, (B + 1) * N, N, dtype=torch.int32, device=Q.device)
+    cu_kv = torch.arange(0, (B + 1) * kv_rows, kv_rows, dtype=torch.int32, device=Q.device)
+    _ancestor(Qr, Kr, Vr, cu_q, N, branching=branching_factor, max_depth=max_depth, parents=par,
+              cu_kv=cu_kv, kv_offset=kv_off,
+              prefix_o=out.view(B * N, Hq, D) if L > 0 else None,
+              prefix_lse=lse.view(B * N, Hq) if L > 0 else None,
+              out=out.view(B * N, Hq, D))
+    return out.permute(0, 2, 1, 3)
+
+
+def _tree_rows(Kt: torch.Tensor, Vt: torch.Tensor, L: int, N: int):
+    """[B, L+N, Hkv, D] views -> ([B*R, Hkv, D] row tensors, R, offset of the tree rows).
+
+    Uses the views directly when the batch stride is a whole number of token
+    rows (the common contiguous [B, L+N, ...] or [B, Hkv, L+N, D] layouts give
+    R = L+N or a larger pitch); otherwise copies the tree rows once.
+    """
+    B, LN, Hkv, D = Kt.shape
+    def rows(t):
+        sb, st = t.stride(0), t.stride(1)
+        if st > 0 and sb % st == 0 and t.stride(3) == 1:
+            R = sb // st
+            # rows past the last sequence's L+N are never addressed
+            base = t.as_strided(((B - 1) * R + LN, Hkv, D), (st, t.stride(2), 1), t.storage_offset())
+            return base, R
+        return None, None
+    Kr, RK = rows(Kt)
+    Vr, RV = rows(Vt)
+    if Kr is not None and Vr is not None and RK == RV:
+        return Kr, Vr, RK, L
+    Kc = Kt[:, L:].contiguous().view(B * N, Hkv, D)
+    Vc = Vt[:, L:].contiguous().view(B * N, Hkv, D)
+    return Kc, Vc, N, 0
