@@ -74,6 +74,17 @@ template <> QA_DEVINL uint32_t pack_pair<__nv_bfloat16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Packed fp32 pair add (sm_100 add.f32x2: one instruction for two lanes).
+QA_DEVINL float2 add2(float2 a, float2 b) {
+  uint64_t r;
+  asm("{.reg .b64 x, y;\n\tmov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
+      "add.rn.f32x2 %0, x, y;\n\t}"
+      : "=l"(r) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  float2 out;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(out.x), "=f"(out.y) : "l"(r));
+  return out;
+}
+
 // Softmax / correction / epilogue role: 4 warps, thread = accumulator row.
 // All tcgen05.ld/st are warp-collective, so every decision that gates them is
 // made warp-uniform (__any_sync / __all_sync).
@@ -97,15 +108,21 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
     tmem_ld32(tl + (j & 1) * kBN + 32, r1);
     tmem_wait_ld();
     const int kvalid = min(kBN, p.prefix_len - j * kBN);  // keys past L were zero-filled
-    float mx = -INFINITY;
+    if (kvalid < kBN) {  // only the last tile is partial
 #pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const float a0 = c < kvalid ? __uint_as_float(r0[c]) * p.scale_log2 : -INFINITY;
-      const float a1 = c + 32 < kvalid ? __uint_as_float(r1[c]) * p.scale_log2 : -INFINITY;
-      r0[c] = __float_as_uint(a0);
-      r1[c] = __float_as_uint(a1);
-      mx = fmaxf(mx, fmaxf(a0, a1));
+      for (int c = 0; c < 32; ++c) {
+        if (c >= kvalid) r0[c] = __float_as_uint(-INFINITY);
+        if (c + 32 >= kvalid) r1[c] = __float_as_uint(-INFINITY);
+      }
     }
+    // row max on raw scores (the scale is positive), scaled once
+    float mx0 = __uint_as_float(r0[0]), mx1 = __uint_as_float(r1[0]);
+#pragma unroll
+    for (int c = 1; c < 32; ++c) {
+      mx0 = fmaxf(mx0, __uint_as_float(r0[c]));
+      mx1 = fmaxf(mx1, __uint_as_float(r1[c]));
+    }
+    const float mx = fmaxf(mx0, mx1) * p.scale_log2;
     const float m_new = fmaxf(m, mx);
     const bool need = m_new > m + kLazy;  // always true on the first tile
     if (j > 0 && __any_sync(0xffffffffu, need)) {
@@ -129,18 +146,20 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
       l *= fast_exp2(m - m_new);
       m = m_new;
     }
+    // p = 2^(s * scale - m): one FMA and one exponential per score
     uint32_t pk[32];
-    float sum = 0.f;
+    float2 acc2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      const float a = fast_exp2(__uint_as_float(r0[2 * c]) - m);
-      const float bb = fast_exp2(__uint_as_float(r0[2 * c + 1]) - m);
-      const float x = fast_exp2(__uint_as_float(r1[2 * c]) - m);
-      const float y = fast_exp2(__uint_as_float(r1[2 * c + 1]) - m);
-      sum += (a + bb) + (x + y);
+      const float a = fast_exp2(fmaf(__uint_as_float(r0[2 * c]), p.scale_log2, -m));
+      const float bb = fast_exp2(fmaf(__uint_as_float(r0[2 * c + 1]), p.scale_log2, -m));
+      const float x = fast_exp2(fmaf(__uint_as_float(r1[2 * c]), p.scale_log2, -m));
+      const float y = fast_exp2(fmaf(__uint_as_float(r1[2 * c + 1]), p.scale_log2, -m));
+      acc2 = add2(acc2, make_float2(a + x, bb + y));
       pk[c] = pack_pair<T>(a, bb);
       pk[16 + c] = pack_pair<T>(x, y);
     }
+    const float sum = acc2.x + acc2.y;
     l += sum;
     tmem_st32(tl + (j & 1) * kBN, pk);  // P_j overwrites the first 32 columns of S_j
     tmem_wait_st();
