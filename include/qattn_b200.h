@@ -152,6 +152,40 @@ typedef struct qa_prefix_args {
 QA_API int qa_prefix_attn(const qa_prefix_args* args, void* stream);
 
 /*
+ * W4A16 GEMM: Y[M, N] (fp16, row stride y_stride) = X[M, K] (fp16, row stride
+ * x_stride) . dequant(W)[K, N], int4 weights with zero point 8, group 128
+ * along K, fp16 scales. Replaces the GPTQModel Marlin W4A16 linears of the
+ * verify step (scripts/w4a16_e2e.py:698-699; checkpoint format
+ * scripts/quantize_llama31.py:41-59: bits=4, group_size=128, sym, no act-order).
+ * Layout: qweight int32 [N, K/8], 8 consecutive k per word with k%8 = 2i in
+ * nibble i and k%8 = 2i+1 in nibble i+4; scales fp16 [K/128, N].
+ * K % 128 == 0, N % 8 == 0, 16-byte aligned pointers.
+ * splits: K split across CTAs (0 = automatic, see qa_w4a16_plan). With more
+ * than one split, `workspace` (fp32, splits*M*N elements, caller-allocated)
+ * holds the partial sums and a second kernel reduces them into Y.
+ */
+typedef struct qa_w4a16_args {
+  const void* x;
+  const int32_t* qweight;
+  const void* scales;
+  void* y;
+  float* workspace; /* required when the resolved split count is > 1 */
+  int64_t x_stride;
+  int64_t y_stride;
+  int32_t M, N, K;
+  int32_t splits; /* 0 = automatic */
+} qa_w4a16_args;
+
+QA_API int qa_w4a16_gemm(const qa_w4a16_args* args, void* stream);
+
+/* Split count chosen by splits = 0, and the workspace bytes it needs. */
+QA_API int qa_w4a16_plan(int32_t M, int32_t N, int32_t K, int32_t* splits, int64_t* workspace_bytes);
+
+/* W'[K, N] (fp16, row-major) = fp16((q - 8) * scale): the dequantisation alone. */
+QA_API int qa_w4a16_dequant(const int32_t* qweight, const void* scales, void* out, int32_t K, int32_t N,
+                            void* stream);
+
+/*
  * Reads and clears the device error flag that the tensor-core kernels set when
  * one of their bounded pipeline waits times out (a kernel that hits it stops,
  * frees its resources and leaves its outputs incomplete). Synchronising call.

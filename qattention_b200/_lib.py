@@ -22,6 +22,9 @@ EXPORTED = (
     "qa_lse_merge",
     "qa_prefix_attn",
     "qa_check_device_error",
+    "qa_w4a16_gemm",
+    "qa_w4a16_plan",
+    "qa_w4a16_dequant",
     "qa_status_string",
     "qa_version",
 )
@@ -65,6 +68,16 @@ class PrefixArgs(Structure):
     ]
 
 
+class W4A16Args(Structure):
+    """Mirror of ``qa_w4a16_args``."""
+
+    _fields_ = [
+        ("x", c_void_p), ("qweight", c_void_p), ("scales", c_void_p), ("y", c_void_p),
+        ("workspace", c_void_p), ("x_stride", c_int64), ("y_stride", c_int64),
+        ("M", c_int32), ("N", c_int32), ("K", c_int32), ("splits", c_int32),
+    ]
+
+
 _LIB = None
 
 
@@ -91,6 +104,12 @@ def lib() -> ctypes.CDLL:
         L.qa_prefix_attn.restype = c_int
         L.qa_check_device_error.argtypes = [POINTER(c_int)]
         L.qa_check_device_error.restype = c_int
+        L.qa_w4a16_gemm.argtypes = [POINTER(W4A16Args), c_void_p]
+        L.qa_w4a16_gemm.restype = c_int
+        L.qa_w4a16_plan.argtypes = [c_int32, c_int32, c_int32, POINTER(c_int32), POINTER(c_int64)]
+        L.qa_w4a16_plan.restype = c_int
+        L.qa_w4a16_dequant.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_void_p]
+        L.qa_w4a16_dequant.restype = c_int
         L.qa_status_string.argtypes = [c_int]
         L.qa_status_string.restype = c_char_p
         L.qa_version.argtypes = []

@@ -442,12 +442,18 @@ extern "C" int qa_prefix_attn(const qa_prefix_args* args, void* stream) {
   return bf ? launch<__nv_bfloat16, 128>(a, st) : launch<__half, 128>(a, st);
 }
 
+namespace qa {
+int w4a16_read_clear_error();  // w4a16_gemm.cu
+}
+
 extern "C" int qa_check_device_error(int* flag) {
   if (flag == nullptr) return QA_ERR_INVALID;
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, qa::g_prefix_error, sizeof(int)) != cudaSuccess) return QA_ERR_LAUNCH;
   if (v != 0 && cudaMemcpyToSymbol(qa::g_prefix_error, &zero, sizeof(int)) != cudaSuccess)
     return QA_ERR_LAUNCH;
-  *flag = v;
+  const int w = qa::w4a16_read_clear_error();
+  if (w < 0) return QA_ERR_LAUNCH;
+  *flag = v | w;
   return QA_OK;
 }

@@ -1,0 +1,109 @@
+"""W4A16 weight format: symmetric int4, group 128 along K, fp16 scales (host-side quantiser).
+
+The reference quantises its verify-step linears with GPTQModel
+``QuantizeConfig(bits=4, group_size=128, desc_act=False, sym=True)``
+(scripts/quantize_llama31.py:41-59) and runs them with Marlin kernels
+(scripts/w4a16_e2e.py:698-699). Neither package ships with the reference, so
+this module states the format it implements, following the published
+symmetric GPTQ rule (round-to-nearest; the GPTQ error-compensating solve is a
+calibration step, out of scope for random-init weights):
+
+* For output column n and group g (k in [128 g, 128 g + 128)):
+  ``amax = max |W[k, n]|`` (an all-zero group uses amax = 1),
+  ``scale = fp16(2 * amax / 15)``, zero point 8 (no zero tensor).
+* ``q = clamp(round_half_even(W / scale) + 8, 0, 15)`` computed in fp32 with
+  the fp16-rounded scale.
+* Dequantisation: ``w = fp16((q - 8) * scale)`` (exact product, one rounding).
+
+Packing (this library's layout, chosen for the GEMM kernel): ``qweight`` is
+int32 ``[N, K // 8]`` holding 8 consecutive k values of one output column per
+word, with the nibbles interleaved: k % 8 = 2i sits in nibble i and
+k % 8 = 2i + 1 in nibble i + 4 (i = 0..3), so ``(word >> 4i) & 0x000F000F``
+yields the consecutive pair (2i, 2i+1) as the two halves of a 32-bit lane.
+``scales`` is fp16 ``[K // 128, N]``. No activation-order permutation
+(``desc_act=False``).
+"""
+from __future__ import annotations
+
+import torch
+
+GROUP = 128
+# bit position of k % 8 = 0..7 inside a packed word (interleaved nibble order)
+NIBBLE_SHIFT = (0, 16, 4, 20, 8, 24, 12, 28)
+
+
+def quantize_w4a16(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantise a ``[K, N]`` weight (Y = X @ W) to ``(qweight [N, K/8] int32, scales [K/128, N] fp16)``.
+
+    Runs with torch ops on W's device (CPU or CUDA); the result is identical on both.
+    """
+    K, N = W.shape
+    if K % GROUP != 0:
+        raise ValueError(f"K ({K}) must be a multiple of the group size {GROUP}")
+    Wf = W.float().reshape(K // GROUP, GROUP, N)
+    amax = Wf.abs().amax(dim=1)                                 # [K/128, N]
+    amax = torch.where(amax == 0, torch.ones_like(amax), amax)
+    scales = (2.0 * amax / 15.0).to(torch.float16)              # [K/128, N]
+    q = torch.round(Wf / scales.float()[:, None, :]) + 8.0
+    q = q.clamp_(0, 15).to(torch.int32).reshape(K, N)           # [K, N] in 0..15
+    qt = q.t().contiguous().view(N, K // 8, 8)                  # [N, K/8, 8], k % 8 last
+    shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=W.device)
+    words = (qt.to(torch.int64) << shifts).sum(dim=-1)          # 0 .. 2^32-1
+    qweight = torch.where(words < 2**31, words, words - 2**32).to(torch.int32)
+    return qweight.contiguous(), scales.contiguous()
+
+
+def unpack_int4(qweight: torch.Tensor) -> torch.Tensor:
+    """``[N, K/8]`` int32 -> ``[K, N]`` int32 values in 0..15 (host helper)."""
+    N, K8 = qweight.shape
+    w = qweight.to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=qweight.device)
+    vals = (w[..., None] >> shifts) & 0xF                         # [N, K/8, 8]
+    return vals.reshape(N, K8 * 8).t().to(torch.int32).contiguous()
+
+
+def w4a16_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                 splits: int = 0, out: torch.Tensor = None) -> torch.Tensor:
+    """``x @ dequant(qweight, scales)`` on the B200 tensor cores (fp16 in/out, fp32 accumulate).
+
+    x: ``[..., K]`` fp16 CUDA (unit stride along K); qweight ``[N, K/8]`` int32,
+    scales ``[K/128, N]`` fp16 (see :func:`quantize_w4a16`). ``splits`` = K split
+    across CTAs (0 = automatic); a split-K run uses a temporary fp32 workspace.
+    """
+    import ctypes
+    from . import _lib
+    if x.dtype != torch.float16 or not x.is_cuda:
+        raise RuntimeError("w4a16_linear needs fp16 CUDA activations")
+    K = x.shape[-1]
+    N = qweight.shape[0]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    y = out if out is not None else torch.empty(M, N, dtype=torch.float16, device=x.device)
+    L = _lib.lib()
+    s = ctypes.c_int32(splits)
+    ws_bytes = ctypes.c_int64(0)
+    if splits == 0 and M > 0:
+        _lib.check(L.qa_w4a16_plan(M, N, K, ctypes.byref(s), ctypes.byref(ws_bytes)), "qa_w4a16_plan")
+    elif splits > 1:
+        ws_bytes.value = splits * M * N * 4
+    ws = torch.empty(max(1, ws_bytes.value // 4), dtype=torch.float32, device=x.device) if ws_bytes.value else None
+    a = _lib.W4A16Args()
+    a.x, a.qweight, a.scales, a.y = x2.data_ptr(), qweight.data_ptr(), scales.data_ptr(), y.data_ptr()
+    a.workspace = ws.data_ptr() if ws is not None else None
+    a.x_stride, a.y_stride = x2.stride(0), y.stride(0)
+    a.M, a.N, a.K, a.splits = M, N, K, s.value
+    _lib.check(L.qa_w4a16_gemm(a, torch.cuda.current_stream(x.device).cuda_stream), "qa_w4a16_gemm")
+    return y.view(*x.shape[:-1], N)
+
+
+def w4a16_dequantize(qweight: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """GPU dequantisation to fp16 ``[K, N]`` (for checks; the GEMM never materialises it)."""
+    from . import _lib
+    N, K8 = qweight.shape
+    out = torch.empty(K8 * 8, N, dtype=torch.float16, device=qweight.device)
+    _lib.check(_lib.lib().qa_w4a16_dequant(qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), K8 * 8, N,
+                                            torch.cuda.current_stream(qweight.device).cuda_stream),
+               "qa_w4a16_dequant")
+    return out

@@ -1,0 +1,54 @@
+"""GPU W4A16: dequantisation bit-exact vs the CPU spec, GEMM vs the fp32 oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import w4a16_oracle as wo
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from qattention_b200 import _lib, quant
+
+
+def _weights(K, N, seed):
+    g = torch.Generator().manual_seed(seed)
+    W = torch.randn(K, N, generator=g) * 0.02
+    qw, sc = quant.quantize_w4a16(W)
+    return qw, sc
+
+
+@pytest.mark.parametrize("K,N", [(128, 128), (512, 384), (4096, 1024)])
+def test_dequant_bit_exact(K, N):
+    qw, sc = _weights(K, N, K + N)
+    out = quant.w4a16_dequantize(qw.cuda(), sc.cuda()).cpu()
+    ref = wo.dequantize(quant.unpack_int4(qw).numpy().astype(np.uint8), sc.numpy())
+    assert np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("M,N,K,splits", [
+    (1, 128, 128, 1), (7, 256, 512, 0), (64, 384, 1024, 1), (128, 128, 4096, 0),
+    (200, 512, 2048, 1), (200, 512, 2048, 4), (1024, 1024, 4096, 0), (33, 4096, 4096, 0),
+])
+def test_gemm_vs_oracle(M, N, K, splits):
+    qw, sc = _weights(K, N, M * 7 + N)
+    g = torch.Generator().manual_seed(M)
+    X = torch.randn(M, K, generator=g).half()
+    Y = quant.w4a16_linear(X.cuda(), qw.cuda(), sc.cuda(), splits=splits).float().cpu()
+    ref = torch.from_numpy(wo.gemm(X.numpy(), quant.unpack_int4(qw).numpy().astype(np.uint8), sc.numpy()))
+    assert _lib.device_error() == 0
+    scale = ref.abs().max().item() + 1e-6
+    err = (Y - ref).abs().max().item()
+    # fp16 output rounding (2^-11 relative) plus fp32 accumulation order
+    assert err <= 2e-3 * scale + 1e-3, f"max err {err:.3e} (max |ref| {scale:.3e})"
+
+
+def test_gemm_strided_activations():
+    K, N, M = 1024, 256, 96
+    qw, sc = _weights(K, N, 5)
+    g = torch.Generator().manual_seed(9)
+    big = torch.randn(M, 2 * K, generator=g).half().cuda()
+    X = big[:, :K]  # row stride 2K
+    Y = quant.w4a16_linear(X, qw.cuda(), sc.cuda())
+    Y2 = quant.w4a16_linear(X.contiguous(), qw.cuda(), sc.cuda())
+    assert torch.equal(Y, Y2)
