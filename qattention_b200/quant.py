@@ -16,12 +16,15 @@ calibration step, out of scope for random-init weights):
 * Dequantisation: ``w = fp16((q - 8) * scale)`` (exact product, one rounding).
 
 Packing (this library's layout, chosen for the GEMM kernel): ``qweight`` is
-int32 ``[N, K // 8]`` holding 8 consecutive k values of one output column per
-word, with the nibbles interleaved: k % 8 = 2i sits in nibble i and
-k % 8 = 2i + 1 in nibble i + 4 (i = 0..3), so ``(word >> 4i) & 0x000F000F``
-yields the consecutive pair (2i, 2i+1) as the two halves of a 32-bit lane.
-``scales`` is fp16 ``[K // 128, N]``. No activation-order permutation
-(``desc_act=False``).
+int32 ``[N // 128, K // 128, 128, 16]`` — tile-major, so the 128 output
+columns x 128 k of one GEMM step are one contiguous 8 KB block that a single
+bulk copy fetches. Inside a tile, row j is output column 128 * tile + j and
+word w holds k = 8 w .. 8 w + 7 of that step with the nibbles interleaved:
+k % 8 = 2i sits in nibble i and k % 8 = 2i + 1 in nibble i + 4 (i = 0..3),
+so ``(word >> 4i) & 0x000F000F`` yields the consecutive pair (2i, 2i+1) as the
+two halves of a 32-bit lane. ``scales`` is fp16 ``[K // 128, N]``. No
+activation-order permutation (``desc_act=False``). N and K are multiples of
+128.
 """
 from __future__ import annotations
 
@@ -33,13 +36,14 @@ NIBBLE_SHIFT = (0, 16, 4, 20, 8, 24, 12, 28)
 
 
 def quantize_w4a16(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Quantise a ``[K, N]`` weight (Y = X @ W) to ``(qweight [N, K/8] int32, scales [K/128, N] fp16)``.
+    """Quantise a ``[K, N]`` weight (Y = X @ W) to
+    ``(qweight [N/128, K/128, 128, 16] int32, scales [K/128, N] fp16)``.
 
     Runs with torch ops on W's device (CPU or CUDA); the result is identical on both.
     """
     K, N = W.shape
-    if K % GROUP != 0:
-        raise ValueError(f"K ({K}) must be a multiple of the group size {GROUP}")
+    if K % GROUP != 0 or N % 128 != 0:
+        raise ValueError(f"K ({K}) and N ({N}) must be multiples of 128")
     Wf = W.float().reshape(K // GROUP, GROUP, N)
     amax = Wf.abs().amax(dim=1)                                 # [K/128, N]
     amax = torch.where(amax == 0, torch.ones_like(amax), amax)
@@ -49,14 +53,16 @@ def quantize_w4a16(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     qt = q.t().contiguous().view(N, K // 8, 8)                  # [N, K/8, 8], k % 8 last
     shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=W.device)
     words = (qt.to(torch.int64) << shifts).sum(dim=-1)          # 0 .. 2^32-1
-    qweight = torch.where(words < 2**31, words, words - 2**32).to(torch.int32)
-    return qweight.contiguous(), scales.contiguous()
+    words = torch.where(words < 2**31, words, words - 2**32).to(torch.int32)  # [N, K/8]
+    qweight = words.view(N // 128, 128, K // 128, 16).permute(0, 2, 1, 3).contiguous()
+    return qweight, scales.contiguous()
 
 
 def unpack_int4(qweight: torch.Tensor) -> torch.Tensor:
-    """``[N, K/8]`` int32 -> ``[K, N]`` int32 values in 0..15 (host helper)."""
-    N, K8 = qweight.shape
-    w = qweight.to(torch.int64) & 0xFFFFFFFF
+    """Tile-major ``[N/128, K/128, 128, 16]`` int32 -> ``[K, N]`` int32 values in 0..15 (host helper)."""
+    NT, KT = qweight.shape[:2]
+    N, K8 = NT * 128, KT * 16
+    w = qweight.permute(0, 2, 1, 3).reshape(N, K8).to(torch.int64) & 0xFFFFFFFF
     shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=qweight.device)
     vals = (w[..., None] >> shifts) & 0xF                         # [N, K/8, 8]
     return vals.reshape(N, K8 * 8).t().to(torch.int32).contiguous()
@@ -75,7 +81,7 @@ def w4a16_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     if x.dtype != torch.float16 or not x.is_cuda:
         raise RuntimeError("w4a16_linear needs fp16 CUDA activations")
     K = x.shape[-1]
-    N = qweight.shape[0]
+    N = qweight.shape[0] * 128
     x2 = x.reshape(-1, K)
     if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
         x2 = x2.contiguous()
@@ -101,9 +107,9 @@ def w4a16_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
 def w4a16_dequantize(qweight: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     """GPU dequantisation to fp16 ``[K, N]`` (for checks; the GEMM never materialises it)."""
     from . import _lib
-    N, K8 = qweight.shape
-    out = torch.empty(K8 * 8, N, dtype=torch.float16, device=qweight.device)
-    _lib.check(_lib.lib().qa_w4a16_dequant(qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), K8 * 8, N,
+    N, K = qweight.shape[0] * 128, qweight.shape[1] * 128
+    out = torch.empty(K, N, dtype=torch.float16, device=qweight.device)
+    _lib.check(_lib.lib().qa_w4a16_dequant(qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), K, N,
                                             torch.cuda.current_stream(qweight.device).cuda_stream),
                "qa_w4a16_dequant")
     return out

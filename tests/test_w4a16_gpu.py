@@ -27,7 +27,7 @@ def test_dequant_bit_exact(K, N):
 
 
 @pytest.mark.parametrize("M,N,K,splits", [
-    (1, 128, 128, 1), (7, 256, 512, 0), (64, 384, 1024, 1), (128, 128, 4096, 0),
+    (1, 128, 128, 1), (7, 256, 512, 0), (16, 256, 512, 1), (40, 256, 512, 2), (64, 384, 1024, 1), (65, 256, 512, 0), (128, 128, 4096, 0),
     (200, 512, 2048, 1), (200, 512, 2048, 4), (1024, 1024, 4096, 0), (33, 4096, 4096, 0),
 ])
 def test_gemm_vs_oracle(M, N, K, splits):

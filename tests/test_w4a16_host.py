@@ -8,12 +8,12 @@ from qattention_b200 import quant
 
 def test_quantiser_matches_oracle_bit_exact():
     g = torch.Generator().manual_seed(0)
-    W = torch.randn(512, 96, generator=g) * 0.05
+    W = torch.randn(512, 128, generator=g) * 0.05
     W[:128, 3] = 0.0  # an all-zero group
     qw, sc = quant.quantize_w4a16(W)
     q_ref, s_ref = wo.quantize(W.numpy())
-    assert qw.dtype == torch.int32 and qw.shape == (96, 512 // 8)
-    assert sc.dtype == torch.float16 and sc.shape == (4, 96)
+    assert qw.dtype == torch.int32 and qw.shape == (1, 4, 128, 16)
+    assert sc.dtype == torch.float16 and sc.shape == (4, 128)
     assert np.array_equal(sc.numpy().view(np.uint16), s_ref.view(np.uint16))
     assert np.array_equal(qw.numpy(), wo.pack(q_ref))
     assert np.array_equal(quant.unpack_int4(qw).numpy(), q_ref.astype(np.int32))
