@@ -179,6 +179,22 @@ typedef struct qa_w4a16_args {
 
 QA_API int qa_w4a16_gemm(const qa_w4a16_args* args, void* stream);
 
+/*
+ * qa_w4a16_gemm without any device allocation, for callers that cannot call
+ * cudaMalloc on their hot path (a host framework that only hands out buffers it
+ * owns, or a serving loop where an allocation's implicit device synchronisation
+ * would stall other streams). No counterpart in the reference.
+ * The split-K partial sums go to a fixed 16 MiB array inside the library
+ * (4 Mi floats: splits * M * N must not exceed it, else QA_ERR_INVALID); every
+ * GPU that loads the library holds that array until the process exits.
+ * `workspace` in args is ignored. The first call on each device looks up the
+ * array's device address (make that first call before any stream capture).
+ * All calls share the array: calls that overlap on the GPU (other streams,
+ * other threads) race on it and must be serialised by the caller.
+ * Calls no cudaMalloc / cudaFree and no allocating library routine.
+ */
+QA_API int qa_w4a16_gemm_noalloc(const qa_w4a16_args* args, void* stream);
+
 /* Split count chosen by splits = 0, and the workspace bytes it needs. */
 QA_API int qa_w4a16_plan(int32_t M, int32_t N, int32_t K, int32_t* splits, int64_t* workspace_bytes);
 

@@ -25,6 +25,7 @@ EXPORTED = (
     "qa_w4a16_gemm",
     "qa_w4a16_plan",
     "qa_w4a16_dequant",
+    "qa_w4a16_gemm_noalloc",
     "qa_status_string",
     "qa_version",
 )
@@ -106,6 +107,8 @@ def lib() -> ctypes.CDLL:
         L.qa_check_device_error.restype = c_int
         L.qa_w4a16_gemm.argtypes = [POINTER(W4A16Args), c_void_p]
         L.qa_w4a16_gemm.restype = c_int
+        L.qa_w4a16_gemm_noalloc.argtypes = [POINTER(W4A16Args), c_void_p]
+        L.qa_w4a16_gemm_noalloc.restype = c_int
         L.qa_w4a16_plan.argtypes = [c_int32, c_int32, c_int32, POINTER(c_int32), POINTER(c_int64)]
         L.qa_w4a16_plan.restype = c_int
         L.qa_w4a16_dequant.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_void_p]

@@ -499,3 +499,57 @@ extern "C" int qa_w4a16_dequant(const int32_t* qweight, const void* scales, void
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
 
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of qa_w4a16_gemm.
+//
+// The split-K path needs an fp32 workspace for its partial sums. Callers that
+// cannot allocate device memory on their hot path get this entry point
+// instead; its workspace is the fixed array below, which every GPU that loads
+// this library holds until the process exits.
+// ---------------------------------------------------------------------------
+namespace qa {
+namespace {
+
+constexpr int64_t kNoAllocScratchFloats = int64_t(4) << 20;  // 16 MiB of fp32 partial sums
+static __device__ __align__(256) float g_w4a16_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array for the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+int scratch_for_current_device(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QA_ERR_DEVICE;
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_w4a16_scratch) != cudaSuccess || ptr == nullptr) return QA_ERR_DEVICE;
+    g_scratch_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_scratch_ptr[dev];
+  return QA_OK;
+}
+
+}  // namespace
+}  // namespace qa
+
+extern "C" int qa_w4a16_gemm_noalloc(const qa_w4a16_args* args, void* stream) {
+  using namespace qa;
+  if (args == nullptr) return QA_ERR_INVALID;
+  qa_w4a16_args a = *args;
+  if (a.M < 0 || a.N <= 0 || a.K <= 0 || a.K % 128 != 0 || a.N % 128 != 0 || a.splits < 0) return QA_ERR_INVALID;
+  if (a.M == 0) return QA_OK;
+  // The split count the GEMM will use is at most this (it only ever lowers it).
+  const int splits = a.splits == 0 ? w4a16_auto_splits(a.M, a.N, a.K) : a.splits;
+  if (splits > 1) {
+    if (int64_t(splits) * a.M * a.N > kNoAllocScratchFloats) return QA_ERR_INVALID;  // beyond the fixed scratch
+    float* scratch = nullptr;
+    const int st = scratch_for_current_device(&scratch);
+    if (st != QA_OK) return st;
+    a.workspace = scratch;  // every partial is written before it is read: nothing to clear
+  }
+  a.splits = splits;
+  return qa_w4a16_gemm(&a, stream);
+}
