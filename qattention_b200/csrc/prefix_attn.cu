@@ -13,9 +13,12 @@
 //   * One CTA = 128 packed query rows of one (sequence, KV head): with GQA the
 //     G = Hq/Hkv query heads sharing a KV head are packed as rows (token, g),
 //     so K/V tiles are read once for all of them (no repeat_kv copies).
-//   * TMA (4-D tensor maps over [B, tokens, heads, D], 128-byte swizzle)
-//     streams 64-key K and V tiles through a 4-stage shared-memory ring; the
-//     Q tile is loaded once. No multicast.
+//   * TMA (5-D tensor maps over [B, tokens, heads, D] with D split into its
+//     two 64-element halves, 128-byte swizzle) streams 64-key K and V tiles
+//     through a 4-stage shared-memory ring, one copy per tile (both halves)
+//     and K and V issued by two different threads: a single issuing thread
+//     sustains only a few TMA copies per microsecond. The Q tile is loaded
+//     once. Every copy lands in this CTA's own shared memory only.
 //   * One thread issues tcgen05.mma: S_j = Q K_j^T into one of two TMEM
 //     buffers (fp32, 64 columns), then O += P_{j-1} V_{j-1} with P read from
 //     TMEM (the fp16/bf16 probabilities overwrite their S buffer) and V from
@@ -42,7 +45,7 @@ namespace {
 constexpr int kBM = 128;    // packed query rows per CTA (= TMEM lanes)
 constexpr int kBN = 64;     // keys per tile
 constexpr int kStages = 4;  // K/V ring depth
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;  // warps 0-3 softmax, 4 Q/K producer, 5 MMA, 6 V producer
 constexpr uint32_t kTmemCols = 256;  // 2 x S (64) + O (<= 128)
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr float kLazy = 8.f;
@@ -203,7 +206,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap k_map,
                        const __grid_constant__ CUtensorMap v_map, const PfxParams p) {
   using namespace sm100;
-  constexpr int NB64 = D / 64;  // 128-byte column blocks per row
   constexpr uint32_t FMT = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -229,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     mbar_init(&bar_q, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bar_kv_full[s], 1);
+      mbar_init(&bar_kv_full[s], 2);  // K producer + V producer
       mbar_init(&bar_kv_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -251,30 +253,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = tmem_base_sh;
   const uint32_t tmem_o = tbase + 2 * kBN;
 
-  if (warp == 4) {
-    // ---------------- TMA producer ----------------
+  if (warp == 4 || warp == 6) {
+    // ---------------- TMA producers: Q once + K tiles (warp 4), V tiles (warp 6) ----------------
     if (lane == 0) {
-      prefetch_tensormap(&q_map);
-      prefetch_tensormap(&k_map);
-      prefetch_tensormap(&v_map);
-      mbar_arrive_expect_tx(&bar_q, PfxSmem<D>::Q_BYTES);
-      for (int r = 0; r < NB64; ++r)
-        tma_load_4d(sQ + r * kBM * 128, &q_map, &bar_q, r * 64, hk * G, n0, b);
+      const bool is_k = warp == 4;
+      const CUtensorMap* map = is_k ? &k_map : &v_map;
+      prefetch_tensormap(map);
+      if (is_k) {
+        prefetch_tensormap(&q_map);
+        mbar_arrive_expect_tx(&bar_q, PfxSmem<D>::Q_BYTES);
+        tma_load_5d(sQ, &q_map, &bar_q, 0, hk * G, n0, 0, b);
+      }
       int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % kStages;
         if (j >= kStages && !mbar_wait(&bar_kv_empty[st], ((j / kStages) - 1) & 1, &abort_flag, kWaitLimit))
           break;
-        mbar_arrive_expect_tx(&bar_kv_full[st], 2 * PfxSmem<D>::KV_BYTES);
-        for (int r = 0; r < NB64; ++r) {
-          tma_load_4d(sK(st) + r * kBN * 128, &k_map, &bar_kv_full[st], r * 64, hk, j * kBN, b);
-          tma_load_4d(sV(st) + r * kBN * 128, &v_map, &bar_kv_full[st], r * 64, hk, j * kBN, b);
-        }
+        // K and V of a stage each add their bytes to the stage's barrier (2 arrivals)
+        mbar_arrive_expect_tx(&bar_kv_full[st], PfxSmem<D>::KV_BYTES);
+        tma_load_5d(is_k ? sK(st) : sV(st), map, &bar_kv_full[st], 0, hk, j * kBN, 0, b);
         issued = j + 1;
       }
       if (abort_flag) {
         // drain: the copies already issued must land before shared memory is released
-        mbar_wait(&bar_q, 0, &abort_flag, kWaitLimit);
+        if (is_k) mbar_wait(&bar_q, 0, &abort_flag, kWaitLimit);
         for (int j = max(0, issued - kStages); j < issued; ++j) {
           uint32_t n = 0;
           while (!mbar_try_wait(&bar_kv_full[j % kStages], (j / kStages) & 1) && ++n < kWaitLimit) {}
@@ -355,20 +357,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 4-D tensor map over [batch, tokens, heads, D] (innermost first), 128-byte
-// swizzled boxes of (64 elements, box_h heads, box_t tokens, 1 sequence).
+// 5-D tensor map over [batch, tokens, heads, D] with D split into 64-element
+// halves, dims (innermost first): d within half, heads, tokens, half, batch.
+// A box of (64, box_h, box_t, D/64, 1) lands as D/64 column blocks, each
+// [box_h * box_t rows][128 B] with the 128-byte swizzle the UMMA descriptors expect.
 bool make_map(CUtensorMap* map, const void* ptr, bool bf16, int D, int heads, int tokens, int batch,
               int64_t stride_h, int64_t stride_t, int64_t stride_b, int box_h, int box_t) {
-  const cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(heads), cuuint64_t(tokens), cuuint64_t(batch)};
-  const cuuint64_t strides[3] = {cuuint64_t(stride_h) * 2, cuuint64_t(stride_t) * 2, cuuint64_t(stride_b) * 2};
-  const cuuint32_t box[4] = {64u, cuuint32_t(box_h), cuuint32_t(box_t), 1u};
-  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  for (int i = 0; i < 3; ++i)
+  const cuuint64_t dims[5] = {64u, cuuint64_t(heads), cuuint64_t(tokens), cuuint64_t(D / 64), cuuint64_t(batch)};
+  const cuuint64_t strides[4] = {cuuint64_t(stride_h) * 2, cuuint64_t(stride_t) * 2, 128u, cuuint64_t(stride_b) * 2};
+  const cuuint32_t box[5] = {64u, cuuint32_t(box_h), cuuint32_t(box_t), cuuint32_t(D / 64), 1u};
+  const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
+  for (int i = 0; i < 4; ++i)
     if (strides[i] % 16 != 0 || strides[i] == 0) return false;
   const auto encode = encode_fn();
   if (encode == nullptr) return false;
   const CUresult r = encode(
-      map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+      map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
       const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
