@@ -357,6 +357,13 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def _finish():
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -373,6 +380,7 @@ def main():
         run_reference(args)
     else:
         run_ours(args)
+    _finish()
 
 
 if __name__ == "__main__":

@@ -22,6 +22,7 @@
 //     back through the same shared region as 16-byte row vectors.
 // Used when every walk level of a tile fits in shared memory (always true for
 // b >= 2; chains up to depth ~300), for head_dim 64, 128 and 256.
+#include <atomic>
 #include "ancestor_plan.cuh"
 
 namespace qa {
@@ -41,6 +42,7 @@ struct TcParams {
   int32_t rows_cap;
   int32_t kw_cap;  // key-list columns per warp (multiple of 16)
   int32_t heads_per_cta;
+  int32_t num_sms;  // host-side launch planning only
   FastDiv div_b;
 };
 
@@ -97,8 +99,10 @@ template <int D> struct TcSmem {
   __host__ __device__ static int total(int rows) { return tok_off(rows) + rows * 16; }
 };
 
-template <typename T, int D, int NBK>
-__global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams p) {
+// MINB = CTAs per SM the register allocation must allow (1, 3 or 4; chosen
+// per launch by launch_tc_minb).
+template <typename T, int D, int NBK, int MINB>
+__global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcParams p) {
   using SM = TcSmem<D>;
   constexpr int RC = D / 8;   // 16-byte chunks per row
   constexpr int KB = D / 16;  // k16 steps of q.k
@@ -349,6 +353,7 @@ __global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams 
   }
 
   // ---- epilogue: normalise, stage the tile in this warp's Q rows, store ----
+  {
 #pragma unroll
   for (int j = 0; j < NB; ++j) {
     *reinterpret_cast<uint32_t*>(sQ + swz<D>(wrow + g, j) + 4 * t) = pack2<T>(o[j][0] * inv0, o[j][1] * inv0);
@@ -361,33 +366,72 @@ __global__ void __launch_bounds__(kTcThreads) ancestor_tc_kernel(const TcParams 
     const uint4 v = *reinterpret_cast<const uint4*>(sQ + swz<D>(wrow + r, c));
     st_stream(Oh + (int64_t(q0) + wq_lo + r) * a.o_stride_t + c * 8, v);
   }
+  }
   }  // wn > 0
   __syncthreads();  // shared tiles are overwritten by the next head
   }  // heads
 }
 
+// Resident CTAs per SM of one instantiation at this shared-memory size
+// (memoised: the size depends only on the tree shape).
+template <typename T, int D, int NBK, int MINB>
+int resident_ctas(int smem) {
+  // (smem << 32 | occupancy) of the last query; atomic so that host threads
+  // launching concurrently read a consistent pair
+  static std::atomic<int64_t> memo{-1};
+  const int64_t m = memo.load(std::memory_order_relaxed);
+  if (m >= 0 && int(m >> 32) == smem) return int(m & 0xffffffff);
+  {
+    if (cudaFuncSetAttribute(ancestor_tc_kernel<T, D, NBK, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kTcMaxSmem) != cudaSuccess)
+      return 0;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ancestor_tc_kernel<T, D, NBK, MINB>, kTcThreads,
+                                                      smem) != cudaSuccess)
+      return 0;
+    memo.store((int64_t(smem) << 32) | int64_t(occ), std::memory_order_relaxed);
+    return occ;
+  }
+}
+
+template <typename T, int D, int NBK, int MINB>
+int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st) {
+  ancestor_tc_kernel<T, D, NBK, MINB><<<dim3{unsigned(blocks)}, kTcThreads, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
+}
+
+// Picks the register budget. The kernel is latency-bound, so resident warps
+// count: the builds capped for 3 and 4 CTAs per SM (168 and 128 registers,
+// some spills) win when they need fewer waves of CTAs than the unconstrained
+// build; among builds with equal waves the one with more registers (fewer
+// spills) runs faster. head_dim 256 is held to <= 2 CTAs by shared memory and
+// uses the unconstrained build only.
 template <typename T, int D, int NBK>
-int launch_tc(TcParams& p, cudaStream_t st) {
+int launch_tc_minb(TcParams& p, cudaStream_t st) {
   const int64_t blocks = int64_t(p.a.batch) * p.tiles_per_seq *
                         ((p.a.num_q_heads + p.heads_per_cta - 1) / p.heads_per_cta);
   if (blocks > 0x7fffffffLL) return QA_ERR_INVALID;
   const int smem = TcSmem<D>::total(p.rows_cap);
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(ancestor_tc_kernel<T, D, NBK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kTcMaxSmem) != cudaSuccess)
-      return QA_ERR_LAUNCH;
-    attr_set = true;
+  auto waves = [&](int occ) -> int64_t {
+    const int64_t slots = int64_t(p.num_sms) * occ;
+    return slots > 0 ? (blocks + slots - 1) / slots : INT64_MAX;
+  };
+  const int64_t w1 = waves(resident_ctas<T, D, NBK, 1>(smem));
+  if constexpr (D <= 128) {
+    const int64_t w3 = waves(resident_ctas<T, D, NBK, 3>(smem));
+    const int64_t w4 = waves(resident_ctas<T, D, NBK, 4>(smem));
+    if (w4 < w3 && w4 < w1) return launch_tc<T, D, NBK, 4>(p, blocks, smem, st);
+    if (w3 < w1) return launch_tc<T, D, NBK, 3>(p, blocks, smem, st);
   }
-  ancestor_tc_kernel<T, D, NBK><<<dim3{unsigned(blocks)}, kTcThreads, smem, st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
+  if (w1 == INT64_MAX) return QA_ERR_LAUNCH;
+  return launch_tc<T, D, NBK, 1>(p, blocks, smem, st);
 }
 
 template <typename T, int D>
 int launch_tc_nbk(TcParams& p, cudaStream_t st) {
-  if (p.kw_cap <= 32) return launch_tc<T, D, 4>(p, st);
-  if (p.kw_cap <= 64) return launch_tc<T, D, 8>(p, st);
-  return launch_tc<T, D, 16>(p, st);
+  if (p.kw_cap <= 32) return launch_tc_minb<T, D, 4>(p, st);
+  if (p.kw_cap <= 64) return launch_tc_minb<T, D, 8>(p, st);
+  return launch_tc_minb<T, D, 16>(p, st);
 }
 
 }  // namespace
@@ -416,9 +460,15 @@ int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
   // heads per CTA: the largest power of two that still leaves >= 2 CTAs per
   // SM (the tile plan is computed once per CTA and reused for its heads)
   {
+    int dev = 0;
+    p.num_sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&p.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return QA_ERR_LAUNCH;
     const int64_t tiles = int64_t(a.batch) * p.tiles_per_seq;
     int hpc = 1;
-    while (hpc * 2 <= a.num_q_heads && tiles * ((a.num_q_heads + 2 * hpc - 1) / (2 * hpc)) >= 2 * 148) hpc *= 2;
+    while (hpc * 2 <= a.num_q_heads && tiles * ((a.num_q_heads + 2 * hpc - 1) / (2 * hpc)) >= 2 * p.num_sms)
+      hpc *= 2;
     p.heads_per_cta = hpc;
   }
   p.div_b = make_fast_div(uint32_t(a.branching));
