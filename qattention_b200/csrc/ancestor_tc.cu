@@ -41,7 +41,6 @@ struct TcParams {
   int32_t head_ratio;
   int32_t rows_cap;
   int32_t kw_cap;  // key-list columns per warp (multiple of 16)
-  int32_t heads_per_cta;
   int32_t num_sms;  // host-side launch planning only
   FastDiv div_b;
 };
@@ -57,6 +56,21 @@ QA_DEVINL void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, 
 QA_DEVINL void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+QA_DEVINL void stsm_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
+}
+QA_DEVINL uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+// 16-byte cp.async.cg to a shared-window address
+QA_DEVINL void cp_async16_s(uint32_t saddr, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gmem) : "memory");
 }
 
 template <typename T> QA_DEVINL void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
@@ -96,7 +110,8 @@ template <int D> struct TcSmem {
   __host__ __device__ static int k_off() { return kTcMQ * D * 2; }
   __host__ __device__ static int v_off(int rows) { return k_off() + rows * D * 2; }
   __host__ __device__ static int tok_off(int rows) { return v_off(rows) + rows * D * 2; }
-  __host__ __device__ static int total(int rows) { return tok_off(rows) + rows * 16; }
+  // + 128: room to align the tiles to 128 bytes
+  __host__ __device__ static int total(int rows) { return tok_off(rows) + rows * 16 + 128; }
 };
 
 // MINB = CTAs per SM the register allocation must allow (1, 3 or 4; chosen
@@ -108,10 +123,12 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   constexpr int KB = D / 16;  // k16 steps of q.k
   constexpr int NB = D / 8;   // n8 blocks of the output
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  unsigned char* sQ = smem_raw;
-  unsigned char* sK = smem_raw + SM::k_off();
-  unsigned char* sV = smem_raw + SM::v_off(p.rows_cap);
-  int64_t* row_off = reinterpret_cast<int64_t*>(smem_raw + SM::tok_off(p.rows_cap));
+  // tiles start on a 128-byte boundary: the unrolled swizzle XORs address bits 4-6
+  unsigned char* smem_base = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  unsigned char* sQ = smem_base;
+  unsigned char* sK = smem_base + SM::k_off();
+  unsigned char* sV = smem_base + SM::v_off(p.rows_cap);
+  int64_t* row_off = reinterpret_cast<int64_t*>(smem_base + SM::tok_off(p.rows_cap));
   __shared__ int lv_off[kMaxLevels];
   __shared__ int win_lo[kMaxLevels + 1];
   __shared__ int win_base[kMaxLevels + 1];
@@ -123,16 +140,23 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   __shared__ int kslot[kWarps][kTcMaxKeys];       // staged K/V row of each key column
 
   const qa_ancestor_args& a = p.a;
-  const int hgroups = (a.num_q_heads + p.heads_per_cta - 1) / p.heads_per_cta;
-  const int h_first = int(blockIdx.x % unsigned(hgroups)) * p.heads_per_cta;
-  const int h_end = min(h_first + p.heads_per_cta, a.num_q_heads);
-  const int rest = int(blockIdx.x / unsigned(hgroups));
-  const int tile = rest % p.tiles_per_seq;
-  const int seq = rest / p.tiles_per_seq;
+  // Persistent, balanced split: the (tile, head) items, tile-major, are cut into
+  // gridDim.x equal contiguous ranges; a CTA plans a tile once for all of its
+  // heads in the range (at most a few tiles per CTA).
+  const int64_t items = int64_t(a.batch) * p.tiles_per_seq * a.num_q_heads;
+  int64_t it = items * blockIdx.x / gridDim.x;
+  const int64_t it_end = items * (blockIdx.x + 1) / gridDim.x;
+  while (it < it_end) {
+  const int64_t tg = it / a.num_q_heads;
+  const int h_first = int(it - tg * a.num_q_heads);
+  const int h_end = int(min(int64_t(a.num_q_heads), h_first + (it_end - it)));
+  it += h_end - h_first;
+  const int tile = int(tg % p.tiles_per_seq);
+  const int seq = int(tg / p.tiles_per_seq);
   const int q0 = __ldg(a.cu_seqlens_q + seq);
   const int len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
   const int q_lo = tile * kTcMQ;
-  if (q_lo >= len) return;  // uniform over the CTA
+  if (q_lo >= len) continue;  // uniform over the CTA
   const int nq = min(kTcMQ, len - q_lo);
   const int kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
   const int tid = threadIdx.x;
@@ -154,8 +178,8 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     int w = 0;
     while (w + 1 < nw && win_base[w + 1] <= j) ++w;
     const int64_t tk = int64_t(kv0) + win_lo[w] + (j - win_base[w]);
-    row_off[2 * j] = tk * a.k_stride_t;
-    row_off[2 * j + 1] = tk * a.v_stride_t;
+    row_off[2 * j] = tk * a.k_stride_t * int64_t(sizeof(T));  // byte offsets
+    row_off[2 * j + 1] = tk * a.v_stride_t * int64_t(sizeof(T));
   }
   // ---- per-warp key list: the warp's level ranges merged into windows ----
   if (lane == 0 && wn > 0) {
@@ -181,7 +205,6 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     }
   }
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t kbase = smem_u32(sK), vbase = smem_u32(sV);
   const int* ks = kslot[warp];
   // ---- which fragment elements are this thread's rows' walk keys ----
   // Row r's step-s key is column w_col[s] + node_s(r); the thread owning
@@ -203,25 +226,33 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     }
   }
   int hk_staged = -1;
+  // Staging: thread tid copies 16-byte chunk my_cc of rows my_r0, my_r0 + RPP,
+  // ...; the swizzle term of those rows is my_x, flipped by kXStep per pass
+  // (RPP is a multiple of 8, or 4 for head_dim 256).
   constexpr int RPP = kTcThreads / RC;
+  constexpr uint32_t kXStep = uint32_t((RPP & 7) << 4);
+  constexpr uint32_t kRowStep = uint32_t(RPP * D * 2);
   const int my_cc = tid % RC, my_r0 = tid / RC;
+  const uint32_t my_x = uint32_t((my_cc ^ (my_r0 & 7)) << 4);
+  const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
   for (int h = h_first; h < h_end; ++h) {
   // ---- stage this head's Q rows, and K/V rows when the KV head changes ----
-  // (each thread always copies the same 16-byte chunk column, RPP rows apart)
   const int hk = h / p.head_ratio;
   {
-    const T* src = reinterpret_cast<const T*>(a.q) + int64_t(h) * a.q_stride_h +
-                   (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8;
-    const int64_t step = int64_t(RPP) * a.q_stride_t;
-    for (int r = my_r0; r < nq; r += RPP, src += step) cp_async16(sQ + swz<D>(r, my_cc), src);
+    const char* src = reinterpret_cast<const char*>(a.q) +
+                      int64_t(sizeof(T)) * (int64_t(h) * a.q_stride_h + (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8);
+    const int64_t step = int64_t(RPP) * a.q_stride_t * int64_t(sizeof(T));
+    uint32_t d = sQa + uint32_t(my_r0 * D * 2), x = my_x;
+    for (int r = my_r0; r < nq; r += RPP, src += step, d += kRowStep, x ^= kXStep) cp_async16_s(d + x, src);
   }
   if (hk != hk_staged) {
-    const T* Kh = reinterpret_cast<const T*>(a.k) + int64_t(hk) * a.k_stride_h + my_cc * 8;
-    const T* Vh = reinterpret_cast<const T*>(a.v) + int64_t(hk) * a.v_stride_h + my_cc * 8;
-    for (int j = my_r0; j < nrows; j += RPP) {
-      const uint32_t d = swz<D>(j, my_cc);
-      cp_async16(sK + d, Kh + row_off[2 * j]);
-      cp_async16(sV + d, Vh + row_off[2 * j + 1]);
+    const char* Kh = reinterpret_cast<const char*>(a.k) + int64_t(sizeof(T)) * (int64_t(hk) * a.k_stride_h + my_cc * 8);
+    const char* Vh = reinterpret_cast<const char*>(a.v) + int64_t(sizeof(T)) * (int64_t(hk) * a.v_stride_h + my_cc * 8);
+    uint32_t d = uint32_t(my_r0 * D * 2), x = my_x;
+    for (int j = my_r0; j < nrows; j += RPP, d += kRowStep, x ^= kXStep) {
+      const longlong2 off = *reinterpret_cast<const longlong2*>(row_off + 2 * j);
+      cp_async16_s(sKa + d + x, Kh + off.x);
+      cp_async16_s(sVa + d + x, Vh + off.y);
     }
     hk_staged = hk;
   }
@@ -229,17 +260,24 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   __syncthreads();
   if (wn > 0) {
   // ---- S = Q . K_list^T over every level's keys at once (registers) ----
+  // A-operand (and stmatrix) lane address of 16x16 block kk of this warp's
+  // rows: row wrow + (lane & 15), chunk 2kk + (lane >> 4), i.e.
+  // q_off ^ ((kk & 3) << 5) plus 128 bytes per 4 blocks (swizzle unrolled).
+  const uint32_t q_off = sQa + uint32_t((wrow + (lane & 15)) * D * 2) + uint32_t((((lane >> 4) ^ (lane & 7))) << 4);
   uint32_t qf[KB][4];
 #pragma unroll
   for (int kk = 0; kk < KB; ++kk)
-    ldsm_x4(smem_u32(sQ) + swz<D>(wrow + (lane & 15), 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1],
-            qf[kk][2], qf[kk][3]);
+    ldsm_x4((q_off ^ uint32_t((kk & 3) << 5)) + uint32_t((kk >> 2) * 128), qf[kk][0], qf[kk][1], qf[kk][2],
+            qf[kk][3]);
   float sc[NBK][4];
-  int kslot_nb[NBK];
+  // B-operand lane address of key block nb: row kslot, chunk 4k2 + (lane >> 3)
+  // = k_off[nb] ^ ((k2 & 1) << 6) plus 128 bytes per 2 steps
+  uint32_t k_off[NBK];
 #pragma unroll
   for (int nb = 0; nb < NBK; ++nb) {
     sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
-    kslot_nb[nb] = 8 * nb < kpad ? ks[8 * nb + (lane & 7)] : 0;
+    const int row = 8 * nb < kpad ? ks[8 * nb + (lane & 7)] : 0;
+    k_off[nb] = uint32_t(row * D * 2) + uint32_t(((lane >> 3) ^ (row & 7)) << 4);
   }
 #pragma unroll
   for (int k2 = 0; k2 < KB / 2; ++k2) {  // k outer: NBK independent accumulation chains
@@ -247,7 +285,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     for (int nb = 0; nb < NBK; ++nb) {
       if (8 * nb < kpad) {
         uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + swz<D>(kslot_nb[nb], 4 * k2 + (lane >> 3)), b0, b1, b2, b3);
+        ldsm_x4(sKa + (k_off[nb] ^ uint32_t((k2 & 1) << 6)) + uint32_t((k2 >> 1) * 128), b0, b1, b2, b3);
         mma16816<T>(sc[nb], qf[2 * k2], b0, b1);
         mma16816<T>(sc[nb], qf[2 * k2 + 1], b2, b3);
       }
@@ -311,38 +349,46 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       const int r = g + 8 * half;
       const float wgt = half ? wp1 : wp0;
       if (r >= wn || wgt == 0.f) continue;
+      const float wgt_n = wgt * (half ? inv1 : inv0);
       const int64_t tq = int64_t(q0) + wq_lo + r;
       const T* po = reinterpret_cast<const T*>(a.prefix_o) + tq * a.prefix_o_stride_t + int64_t(h) * a.prefix_o_stride_h;
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
         const float2 f = pair_to_f32<T>(__ldg(reinterpret_cast<const unsigned int*>(po + 8 * j + 2 * t)));
-        o[j][2 * half] = wgt * f.x;
-        o[j][2 * half + 1] = wgt * f.y;
+        o[j][2 * half] = wgt_n * f.x;
+        o[j][2 * half + 1] = wgt_n * f.y;
       }
     }
   }
 #pragma unroll
   for (int kp = 0; kp < NBK / 2; ++kp) {
     if (16 * kp >= kpad) break;
+    // P normalised before rounding to T: O needs no rescale afterwards
+    const float p00 = sc[2 * kp][0] * inv0, p01 = sc[2 * kp][1] * inv0;
+    const float p02 = sc[2 * kp][2] * inv1, p03 = sc[2 * kp][3] * inv1;
+    const float p10 = sc[2 * kp + 1][0] * inv0, p11 = sc[2 * kp + 1][1] * inv0;
+    const float p12 = sc[2 * kp + 1][2] * inv1, p13 = sc[2 * kp + 1][3] * inv1;
     uint32_t pa[4];
-    pa[0] = pack2<T>(sc[2 * kp][0], sc[2 * kp][1]);
-    pa[1] = pack2<T>(sc[2 * kp][2], sc[2 * kp][3]);
-    pa[2] = pack2<T>(sc[2 * kp + 1][0], sc[2 * kp + 1][1]);
-    pa[3] = pack2<T>(sc[2 * kp + 1][2], sc[2 * kp + 1][3]);
+    pa[0] = pack2<T>(p00, p01);
+    pa[1] = pack2<T>(p02, p03);
+    pa[2] = pack2<T>(p10, p11);
+    pa[3] = pack2<T>(p12, p13);
     uint32_t pb[4] = {0u, 0u, 0u, 0u};
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
       // bf16 keeps 8 mantissa bits: the rounding remainder goes in a second product
       auto rem = [](float x) { return x - __bfloat162float(__float2bfloat16_rn(x)); };
-      pb[0] = pack2<T>(rem(sc[2 * kp][0]), rem(sc[2 * kp][1]));
-      pb[1] = pack2<T>(rem(sc[2 * kp][2]), rem(sc[2 * kp][3]));
-      pb[2] = pack2<T>(rem(sc[2 * kp + 1][0]), rem(sc[2 * kp + 1][1]));
-      pb[3] = pack2<T>(rem(sc[2 * kp + 1][2]), rem(sc[2 * kp + 1][3]));
+      pb[0] = pack2<T>(rem(p00), rem(p01));
+      pb[1] = pack2<T>(rem(p02), rem(p03));
+      pb[2] = pack2<T>(rem(p10), rem(p11));
+      pb[3] = pack2<T>(rem(p12), rem(p13));
     }
+    // transposed B-operand lane address: row slot, chunk 2jp + (lane >> 4)
     const int slot = ks[16 * kp + (lane & 7) + 8 * ((lane >> 3) & 1)];
+    const uint32_t v_off = sVa + uint32_t(slot * D * 2) + uint32_t(((lane >> 4) ^ (slot & 7)) << 4);
 #pragma unroll
     for (int jp = 0; jp < D / 16; ++jp) {
       uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(vbase + swz<D>(slot, 2 * jp + (lane >> 4)), b0, b1, b2, b3);
+      ldsm_x4_t((v_off ^ uint32_t((jp & 3) << 5)) + uint32_t((jp >> 2) * 128), b0, b1, b2, b3);
       mma16816<T>(o[2 * jp], pa, b0, b1);
       mma16816<T>(o[2 * jp + 1], pa, b2, b3);
       if constexpr (std::is_same<T, __nv_bfloat16>::value) {
@@ -352,24 +398,32 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     }
   }
 
-  // ---- epilogue: normalise, stage the tile in this warp's Q rows, store ----
-  {
+  // ---- epilogue: stage the tile in this warp's Q rows (stmatrix), store rows ----
 #pragma unroll
-  for (int j = 0; j < NB; ++j) {
-    *reinterpret_cast<uint32_t*>(sQ + swz<D>(wrow + g, j) + 4 * t) = pack2<T>(o[j][0] * inv0, o[j][1] * inv0);
-    *reinterpret_cast<uint32_t*>(sQ + swz<D>(wrow + g + 8, j) + 4 * t) = pack2<T>(o[j][2] * inv1, o[j][3] * inv1);
-  }
+  for (int jj = 0; jj < D / 16; ++jj)
+    stsm_x4((q_off ^ uint32_t((jj & 3) << 5)) + uint32_t((jj >> 2) * 128), pack2<T>(o[2 * jj][0], o[2 * jj][1]),
+            pack2<T>(o[2 * jj][2], o[2 * jj][3]), pack2<T>(o[2 * jj + 1][0], o[2 * jj + 1][1]),
+            pack2<T>(o[2 * jj + 1][2], o[2 * jj + 1][3]));
   __syncwarp();
-  T* Oh = reinterpret_cast<T*>(a.o) + int64_t(h) * a.o_stride_h;
-  for (int i = lane; i < wn * RC; i += 32) {
-    const int r = i / RC, c = i - r * RC;
-    const uint4 v = *reinterpret_cast<const uint4*>(sQ + swz<D>(wrow + r, c));
-    st_stream(Oh + (int64_t(q0) + wq_lo + r) * a.o_stride_t + c * 8, v);
-  }
+  {
+    constexpr int RPI = 32 / RC;  // rows per store instruction (power of two)
+    const int c = lane % RC, r0 = lane / RC;
+    const uint32_t s0 = sQa + uint32_t((wrow + r0) * D * 2) + uint32_t((c ^ r0) << 4);
+    const char* dst = reinterpret_cast<const char*>(a.o) +
+                      int64_t(sizeof(T)) * (int64_t(h) * a.o_stride_h + (int64_t(q0) + wq_lo + r0) * a.o_stride_t + c * 8);
+    const int64_t dstep = int64_t(RPI) * a.o_stride_t * int64_t(sizeof(T));
+#pragma unroll
+    for (int it = 0; it < 16 / RPI; ++it) {
+      // row r0 + it*RPI: (r & 7) = r0 ^ ((it*RPI) & 7) since r0 < RPI
+      if (r0 + it * RPI < wn)
+        st_stream(const_cast<char*>(dst), lds128((s0 ^ uint32_t(((it * RPI) & 7) << 4)) + uint32_t(it * RPI * D * 2)));
+      dst += dstep;
+    }
   }
   }  // wn > 0
   __syncthreads();  // shared tiles are overwritten by the next head
   }  // heads
+  }  // tiles
 }
 
 // Resident CTAs per SM of one instantiation at this shared-memory size
@@ -400,30 +454,29 @@ int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
 
-// Picks the register budget. The kernel is latency-bound, so resident warps
-// count: the builds capped for 3 and 4 CTAs per SM (168 and 128 registers,
-// some spills) win when they need fewer waves of CTAs than the unconstrained
-// build; among builds with equal waves the one with more registers (fewer
-// spills) runs faster. head_dim 256 is held to <= 2 CTAs by shared memory and
-// uses the unconstrained build only.
+// Picks the register budget and the persistent grid (one CTA per resident
+// slot). The kernel is latency-bound, so resident warps count: the builds
+// capped for 3 and 4 CTAs per SM (168 and 128 registers, some spills) are used
+// only when they raise residency; at equal residency the build with more
+// registers (fewer spills) runs faster. head_dim 256 is held to <= 2 CTAs by
+// shared memory and uses the unconstrained build only.
 template <typename T, int D, int NBK>
 int launch_tc_minb(TcParams& p, cudaStream_t st) {
-  const int64_t blocks = int64_t(p.a.batch) * p.tiles_per_seq *
-                        ((p.a.num_q_heads + p.heads_per_cta - 1) / p.heads_per_cta);
-  if (blocks > 0x7fffffffLL) return QA_ERR_INVALID;
+  const int64_t items = int64_t(p.a.batch) * p.tiles_per_seq * p.a.num_q_heads;
   const int smem = TcSmem<D>::total(p.rows_cap);
-  auto waves = [&](int occ) -> int64_t {
-    const int64_t slots = int64_t(p.num_sms) * occ;
-    return slots > 0 ? (blocks + slots - 1) / slots : INT64_MAX;
-  };
-  const int64_t w1 = waves(resident_ctas<T, D, NBK, 1>(smem));
+  const int occ1 = resident_ctas<T, D, NBK, 1>(smem);
+  int occ = occ1, minb = 1;
   if constexpr (D <= 128) {
-    const int64_t w3 = waves(resident_ctas<T, D, NBK, 3>(smem));
-    const int64_t w4 = waves(resident_ctas<T, D, NBK, 4>(smem));
-    if (w4 < w3 && w4 < w1) return launch_tc<T, D, NBK, 4>(p, blocks, smem, st);
-    if (w3 < w1) return launch_tc<T, D, NBK, 3>(p, blocks, smem, st);
+    const int occ3 = resident_ctas<T, D, NBK, 3>(smem);
+    const int occ4 = resident_ctas<T, D, NBK, 4>(smem);
+    if (occ3 > occ) occ = occ3, minb = 3;
+    if (occ4 > occ) occ = occ4, minb = 4;
   }
-  if (w1 == INT64_MAX) return QA_ERR_LAUNCH;
+  if (occ <= 0) return QA_ERR_LAUNCH;
+  const int64_t blocks = min(items, int64_t(p.num_sms) * occ);
+  if (blocks <= 0) return QA_OK;
+  if (minb == 4) return launch_tc<T, D, NBK, 4>(p, blocks, smem, st);
+  if (minb == 3) return launch_tc<T, D, NBK, 3>(p, blocks, smem, st);
   return launch_tc<T, D, NBK, 1>(p, blocks, smem, st);
 }
 
@@ -457,19 +510,11 @@ int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
   p.head_ratio = a.num_q_heads / a.num_kv_heads;
   p.rows_cap = rows;
   p.kw_cap = kw;
-  // heads per CTA: the largest power of two that still leaves >= 2 CTAs per
-  // SM (the tile plan is computed once per CTA and reused for its heads)
   {
     int dev = 0;
-    p.num_sms = 148;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&p.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return QA_ERR_LAUNCH;
-    const int64_t tiles = int64_t(a.batch) * p.tiles_per_seq;
-    int hpc = 1;
-    while (hpc * 2 <= a.num_q_heads && tiles * ((a.num_q_heads + 2 * hpc - 1) / (2 * hpc)) >= 2 * p.num_sms)
-      hpc *= 2;
-    p.heads_per_cta = hpc;
   }
   p.div_b = make_fast_div(uint32_t(a.branching));
   const bool bf = a.dtype == QA_DTYPE_BF16;
