@@ -157,9 +157,10 @@ QA_API int qa_prefix_attn(const qa_prefix_args* args, void* stream);
  * along K, fp16 scales. Replaces the GPTQModel Marlin W4A16 linears of the
  * verify step (scripts/w4a16_e2e.py:698-699; checkpoint format
  * scripts/quantize_llama31.py:41-59: bits=4, group_size=128, sym, no act-order).
- * Layout: qweight int32, tile-major [N/128][K/128][128][16]: each 128-column x
- * 128-k tile is one contiguous 8 KB block, row j = output column, word w =
- * k 8w..8w+7 with k%8 = 2i in nibble i and k%8 = 2i+1 in nibble i+4;
+ * Layout: qweight int32, tile-major [N/128][K/128][4][128][4]: each 128-column x
+ * 128-k tile is one contiguous 8 KB block stored chunk-plane-major: index
+ * [tn][tk][c][j][w] is output column 128 tn + j, word 4c + w of its row, which
+ * holds k = 8 (4c + w) .. + 7 with k%8 = 2i in nibble i and k%8 = 2i+1 in nibble i+4;
  * scales fp16 [K/128, N]. K % 128 == 0, N % 128 == 0, 16-byte aligned pointers.
  * splits: K split across CTAs (0 = automatic, see qa_w4a16_plan). With more
  * than one split, `workspace` (fp32, splits*M*N elements, caller-allocated)

@@ -29,16 +29,18 @@ def quantize(W: np.ndarray):
 
 
 def pack(q: np.ndarray) -> np.ndarray:
-    """q [K, N] 0..15 -> qweight [N/128, K/128, 128, 16] int32 (the library's tile-major
-    layout): 8 consecutive k per word, k%8 = 2i in nibble i and k%8 = 2i+1 in nibble i+4."""
+    """q [K, N] 0..15 -> qweight [N/128, K/128, 4, 128, 4] int32 (the library's tile-major,
+    chunk-plane layout: tile (n tile, k tile), 16-byte chunk c, row = output column, word w
+    holds k = 32 c + 8 w .. + 7): 8 consecutive k per word, k%8 = 2i in nibble i and
+    k%8 = 2i+1 in nibble i+4."""
     K, N = q.shape
     qt = q.T.reshape(N, K // 8, 8).astype(np.uint32)
     words = np.zeros((N, K // 8), dtype=np.uint32)
     for j in range(8):
         nibble = j // 2 if j % 2 == 0 else 4 + j // 2
         words |= qt[:, :, j] << np.uint32(4 * nibble)
-    w = words.view(np.int32).reshape(N // 128, 128, K // 128, 16)
-    return np.ascontiguousarray(w.transpose(0, 2, 1, 3))
+    w = words.view(np.int32).reshape(N // 128, 128, K // 128, 4, 4)
+    return np.ascontiguousarray(w.transpose(0, 2, 3, 1, 4))
 
 
 def dequantize(q: np.ndarray, scales: np.ndarray) -> np.ndarray:

@@ -49,6 +49,31 @@ QA_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint (ns): a waiting thread sleeps until the
+// phase completes (or the hint elapses) instead of spinning on the issue slots
+// that the working warps of its SM sub-partition need.
+QA_DEVINL bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded sleeping wait: at most `limit` tries of up to hint_ns each.
+QA_DEVINL bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t limit,
+                               uint32_t hint_ns = 10000) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+    if (*abort) return false;
+  }
+  *abort = 1;
+  return false;
+}
+
 // Bounded wait: returns false (and sets *abort) when the phase does not
 // complete within `limit` polls or another role has already aborted.
 QA_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t limit) {

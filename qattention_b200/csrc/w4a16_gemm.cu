@@ -1,29 +1,22 @@
-// W4A16 weight-streaming GEMM (kernel G1), sm_100a tcgen05/TMEM.
+// W4A16 weight-streaming GEMM, sm_100a tcgen05/TMEM.
 //
 // Y[M, N] = X[M, K] . dequant(W)[K, N] for int4 weights (symmetric, zero point
 // 8, group 128 along K, one fp16 scale per group and output column) and fp16
 // activations: the verify-step linears that the reference runs as GPTQModel
 // Marlin kernels (scripts/w4a16_e2e.py:698-699, format set by
 // scripts/quantize_llama31.py:41-59). Packed layout: qweight int32, tile-major
-// [N/128][K/128][128][16] (each 8 KB tile of one GEMM step contiguous; 8
-// consecutive k per word, nibbles interleaved so that (w >> 4i) & 0x000F000F is
-// the pair (2i, 2i+1)), scales fp16 [K/128, N].
+// [N/128][K/128][4][128][4] (each 8 KB tile of one GEMM step contiguous and
+// chunk-plane-major inside: 16-byte chunk c of output column j at c*2048 + j*16;
+// 8 consecutive k per word, nibbles interleaved so that bits 0-3|16-19 hold
+// the pair (0,1), 4-7|20-23 (2,3), 8-11|24-27 (4,5), 12-15|28-31 (6,7)),
+// scales fp16 [K/128, N]. Dequantisation w = fp16((q - 8) * scale), one rounding.
 //
-// B200 design (128 x 128 output tile per CTA, 64-deep K steps):
-//   * One bulk copy per step fetches the contiguous 8 KB packed weight tile
-//     (plus a 256-byte TMA of its scales) into a deep ring; TMA streams the
-//     activation tile (128-byte swizzle) into a second ring.
-//   * Four dequantisation warps (thread = output column) expand 64 int4 values
-//     to fp16 in registers — q | 0x6400 reads as 1024 + q, minus 1032 gives
-//     q - 8 exactly, times the fp16 scale is one correctly rounded product —
-//     and write them into a swizzled K-major B tile (double buffered).
-//   * One thread issues tcgen05.mma (M=128, N=128, K=16) with the fp32
-//     accumulator in TMEM; commits free the ring stages and B buffers.
-//   * The dequant warps read the accumulator back (tcgen05.ld) and store fp16
-//     Y, or fp32 partial sums when K is split across CTAs (small M: the grid
-//     needs more CTAs than output tiles); a second kernel reduces the splits.
-//   * HBM-bound for small M (0.5 byte per weight + 2 bytes per 128 weights),
-//     tensor-core-bound for large M. Bounded waits as in the prefix pass.
+// The kernel computes D^T = W^T X^T with the dequantised weights as the A
+// operand in TMEM (see the kernel's comment); it is HBM-bound for small M
+// (0.5 byte per weight + 2 bytes per 128 weights) and tensor-bound for large M.
+// Split-K partial sums (small grids) go to an fp32 workspace that a second
+// kernel reduces. All waits are bounded (iteration caps, abort flag, device
+// error flag read by qa_check_device_error).
 #include "sm100_ptx.cuh"
 
 #include <cudaTypedefs.h>
@@ -35,265 +28,10 @@ __device__ int g_w4a16_error = 0;
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 128;  // one quantisation group per K step
-constexpr int kMaxStages = 8;                     // ring depths are set per launch (<= 8)
-// warps 0-3: weight-ring producers (one thread each, round-robin over K steps:
-// a single issuing thread sustains only a few bulk copies per microsecond),
-// warp 4: activation-ring producer, warp 5: MMA issuer, warps 6-21: dequant.
-constexpr int kProducers = 4;
-constexpr int kXWarp = 4, kMmaWarp = 5, kDeqWarp0 = 6;
-constexpr int kThreads = 704;
-constexpr int kDeqThreads = 512;
-constexpr uint32_t kTmemCols = 128;
-constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr int kWBytes = kBN * (kBK / 8) * 4;    // 8 KB packed
-constexpr int kSBytes = kBN * 2;                // 256 B of scales
-constexpr int kWStageBytes = kWBytes + 1024;    // keep every stage 1 KB aligned
-constexpr int kBBytes = kBN * kBK * 2;          // 32 KB dequantised
-constexpr int kSmem = 220 * 1024;  // dynamic shared memory (static barriers use the rest); rings laid out per launch
-
-struct W4Params {
-  int32_t m_pad;     // swapped mode: X rows per tile (N of the MMA), multiple of 16
-  int32_t x_stages;  // activation ring depth
-  int32_t w_stages;  // packed-weight ring depth
-  int32_t b_bufs;    // dequantised B tiles in flight
-  const uint32_t* qweight;  // tile-major [N/128][K/128][128][16]
-  const __half* scales;     // [K/128][N]
-  void* y;  // fp16 [M, N] (row stride y_stride) or fp32 partials [splits, M, N]
-  int64_t y_stride;
-  int32_t M, N, K;
-  int32_t k_tiles_per_split;
-  int32_t split;  // 1 = direct fp16 output
-};
-
-// SWAP (M <= 64): D^T = W^T X^T, so the dequantised 128-column weight tile is the
-// M=128 A operand and the few activation rows are the narrow B operand; the
-// tensor-core time per weight byte then shrinks with M and the kernel is bound
-// by the weight stream. Otherwise D = X W with 128-row activation tiles.
-template <bool SPLIT, bool SWAP>
-__global__ void __launch_bounds__(kThreads, 1)
-    w4a16_gemm_kernel(const __grid_constant__ CUtensorMap x_map, const W4Params p) {
-  using namespace sm100;
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int x_rows = SWAP ? p.m_pad : kBM;  // activation rows per tile
-  const int x_bytes = x_rows * kBK * 2;
-  const int kXStages = p.x_stages, kWStages = p.w_stages;
-  const int kB = p.b_bufs;
-  auto sB = [&](int b) { return base + b * kBBytes; };
-  auto sW = [&](int st) { return base + kB * kBBytes + st * kWStageBytes; };
-  auto sX = [&](int st) { return base + kB * kBBytes + kWStages * kWStageBytes + st * x_bytes; };
-  auto sS = [&](int st) { return sW(st) + kWBytes; };
-
-  __shared__ __align__(8) uint64_t bar_w_full[kMaxStages], bar_w_empty[kMaxStages];
-  __shared__ __align__(8) uint64_t bar_x_full[kMaxStages], bar_x_empty[kMaxStages];
-  __shared__ __align__(8) uint64_t bar_deq_full[8], bar_deq_empty[8], bar_acc, bar_final;
-  __shared__ uint32_t tmem_base_sh;
-  __shared__ volatile int abort_flag;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int mt = blockIdx.x, nt = blockIdx.y, split = blockIdx.z;
-  const int k_tiles = p.K / kBK;
-  const int kt0 = split * p.k_tiles_per_split;
-  const int kt1 = min(k_tiles, kt0 + p.k_tiles_per_split);
-  const int nk = max(0, kt1 - kt0);
-
-  if (tid == 0) {
-    for (int s = 0; s < kWStages; ++s) {
-      mbar_init(&bar_w_full[s], 1);
-      mbar_init(&bar_w_empty[s], kDeqThreads);
-    }
-    for (int s = 0; s < kXStages; ++s) {
-      mbar_init(&bar_x_full[s], 1);
-      mbar_init(&bar_x_empty[s], 1);
-    }
-    for (int b = 0; b < 8; ++b) {
-      mbar_init(&bar_deq_full[b], kDeqThreads);
-      mbar_init(&bar_deq_empty[b], 1);
-    }
-    mbar_init(&bar_acc, 1);
-    mbar_init(&bar_final, 1);
-    abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == kMmaWarp) {
-    tmem_alloc(&tmem_base_sh, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tacc = tmem_base_sh;
-
-  if (warp < kProducers) {
-    // ---------------- weight ring: packed tile (8 KB) + its scale row (256 B) ----------------
-    if (lane == 0) {
-      int issued = 0;
-      for (int i = warp; i < nk; i += kProducers) {
-        const int st = i % kWStages, kt = kt0 + i;
-        if (i >= kWStages && !mbar_wait(&bar_w_empty[st], ((i / kWStages) - 1) & 1, &abort_flag, kWaitLimit)) break;
-        mbar_arrive_expect_tx(&bar_w_full[st], kWBytes + kSBytes);
-        bulk_load(sW(st), p.qweight + (int64_t(nt) * k_tiles + kt) * (kBN * kBK / 8), kWBytes, &bar_w_full[st]);
-        bulk_load(sS(st), p.scales + int64_t(kt) * p.N + nt * kBN, kSBytes, &bar_w_full[st]);
-        issued = i + 1;
-      }
-      if (abort_flag) {  // let this thread's issued copies land before shared memory is released
-        for (int i = warp; i < issued; i += kProducers) {
-          if (i + kWStages < issued) continue;
-          uint32_t n = 0;
-          while (!mbar_try_wait(&bar_w_full[i % kWStages], (i / kWStages) & 1) && ++n < kWaitLimit) {}
-        }
-      }
-    }
-  } else if (warp == kXWarp) {
-    // ---------------- activation ring: one 3-D TMA per step (both 64-column halves) ----------------
-    if (lane == 0) {
-      prefetch_tensormap(&x_map);
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
-        const int st = i % kXStages, kt = kt0 + i;
-        if (i >= kXStages && !mbar_wait(&bar_x_empty[st], ((i / kXStages) - 1) & 1, &abort_flag, kWaitLimit)) break;
-        mbar_arrive_expect_tx(&bar_x_full[st], x_bytes);
-        tma_load_3d(sX(st), &x_map, &bar_x_full[st], 0, mt * x_rows, kt * 2);
-        issued = i + 1;
-      }
-      if (abort_flag) {
-        for (int i = max(0, issued - kXStages); i < issued; ++i) {
-          uint32_t n = 0;
-          while (!mbar_try_wait(&bar_x_full[i % kXStages], (i / kXStages) & 1) && ++n < kWaitLimit) {}
-        }
-      }
-    }
-  } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc = SWAP ? f16_idesc(0, 0, 0, kBN, uint32_t(x_rows)) : f16_idesc(0, 0, 0, kBM, kBN);
-      for (int i = 0; i < nk; ++i) {
-        const int sx = i % kXStages, b = i % kB;
-        if (!mbar_wait(&bar_x_full[sx], (i / kXStages) & 1, &abort_flag, kWaitLimit)) break;
-        if (!mbar_wait(&bar_deq_full[b], (i / kB) & 1, &abort_flag, kWaitLimit)) break;
-        tc_fence_after();
-        const uint32_t xa = smem_addr(sX(sx)), ba = smem_addr(sB(b));
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint64_t xd = sw128_desc(xa + (kk / 4) * x_rows * 128 + (kk % 4) * 32, 16, 1024);
-          const uint64_t wd = sw128_desc(ba + (kk / 4) * kBN * 128 + (kk % 4) * 32, 16, 1024);
-          if constexpr (SWAP) mma_ss(tacc, wd, xd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-          else mma_ss(tacc, xd, wd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&bar_x_empty[sx]);
-        mma_commit(&bar_deq_empty[b]);
-      }
-      mma_commit(&bar_acc);
-      mma_commit(&bar_final);
-      uint32_t n = 0;
-      while (!mbar_try_wait(&bar_final, 0) && ++n < kWaitLimit) {}
-    }
-  } else if (warp >= kDeqWarp0) {
-    // ---------------- dequantisation: thread = (output column, quarter of the 128 k) ----------------
-    const int t = tid - kDeqWarp0 * 32;  // 0..511
-    const int nrow = t & 127, qk = t >> 7;  // k range [32 qk, 32 qk + 32)
-    const int half = qk & 1;                // epilogue column half (warps 4-7 / 8-11)
-    bool ok = true;
-    for (int i = 0; i < nk; ++i) {
-      const int st = i % kWStages, b = i % kB;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_w_full[st], (i / kWStages) & 1, &abort_flag, kWaitLimit));
-      if (!ok) break;
-      if (i >= kB) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_deq_empty[b], ((i / kB) - 1) & 1, &abort_flag, kWaitLimit));
-        if (!ok) break;
-      }
-      const uint4 w0 = lds128(smem_addr(sW(st)) + nrow * 64 + qk * 16);
-      const __half sc = __ushort_as_half(lds16(smem_addr(sS(st)) + nrow * 2));
-      mbar_arrive(&bar_w_empty[st]);  // packed words and scale are in registers
-      const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
-      const __half2 s2 = __halves2half2(sc, sc);
-      const __half2 bias = __floats2half2_rn(1032.f, 1032.f);
-      // words cover k = 32 qk .. 32 qk + 31: column block qk / 2, chunks 4 (qk % 2) .. +3
-      const uint32_t row = smem_addr(sB(b)) + (qk >> 1) * (kBN * 128) + nrow * 128;
-#pragma unroll
-      for (int cw = 0; cw < 4; ++cw) {
-        const int c = 4 * (qk & 1) + cw;
-        uint32_t o[4];
-#pragma unroll
-        for (int i4 = 0; i4 < 4; ++i4) {
-          const uint32_t bits = ((words[cw] >> (4 * i4)) & 0x000F000Fu) | 0x64006400u;
-          __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&bits), bias);  // q - 8, exact
-          h = __hmul2(h, s2);                                                 // one rounding
-          o[i4] = *reinterpret_cast<uint32_t*>(&h);
-        }
-        sts128(row + ((c ^ (nrow & 7)) * 16), o[0], o[1], o[2], o[3]);
-      }
-      fence_proxy_async_smem();  // make the B tile visible to the tensor cores
-      mbar_arrive(&bar_deq_full[b]);
-    }
-    // ---------------- epilogue: warps 4-7 columns 0-63, warps 8-11 columns 64-127 ----------------
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag, kWaitLimit));
-    if (qk >= 2) ok = false;  // the second eight dequant warps do not take part in the epilogue
-    if (ok && SWAP) {
-      // TMEM lane = output column n, TMEM column = activation row m
-      tc_fence_after();
-      const int quarter = warp & 3;
-      const int n = nt * kBN + quarter * 32 + lane;
-#pragma unroll 1
-      for (int c4 = half; c4 * 32 < x_rows; c4 += 2) {
-        uint32_t acc[32];
-        tmem_ld32(tacc + (uint32_t(quarter * 32) << 16) + c4 * 32, acc);
-        tmem_wait_ld();
-        if (n >= p.N) continue;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int m = mt * x_rows + c4 * 32 + c;
-          if (m >= p.M || c4 * 32 + c >= x_rows) break;
-          if constexpr (SPLIT)
-            reinterpret_cast<float*>(p.y)[(int64_t(split) * p.M + m) * p.N + n] = __uint_as_float(acc[c]);
-          else
-            reinterpret_cast<__half*>(p.y)[int64_t(m) * p.y_stride + n] = __float2half_rn(__uint_as_float(acc[c]));
-        }
-      }
-    } else if (ok) {
-      tc_fence_after();
-      const int quarter = warp & 3;
-      const int row = quarter * 32 + lane;
-      const int m = mt * kBM + row;
-      const bool m_ok = m < p.M;
-#pragma unroll 1
-      for (int c4 = 2 * half; c4 < 2 * half + 2; ++c4) {
-        uint32_t acc[32];
-        tmem_ld32(tacc + (uint32_t(quarter * 32) << 16) + c4 * 32, acc);
-        tmem_wait_ld();
-        const int n0 = nt * kBN + c4 * 32;
-        if (!m_ok || n0 >= p.N) continue;
-        if constexpr (SPLIT) {
-          float* dst = reinterpret_cast<float*>(p.y) + (int64_t(split) * p.M + m) * p.N + n0;
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            reinterpret_cast<uint4*>(dst)[q] = make_uint4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
-        } else {
-          __half* dst = reinterpret_cast<__half*>(p.y) + int64_t(m) * p.y_stride + n0;
-          uint32_t hv[16];
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            __half2 v = __floats2half2_rn(__uint_as_float(acc[2 * c]), __uint_as_float(acc[2 * c + 1]));
-            hv[c] = *reinterpret_cast<uint32_t*>(&v);
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            reinterpret_cast<uint4*>(dst)[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc(tacc, kTmemCols);
-  }
-  if (tid == 0 && abort_flag) atomicExch(&g_w4a16_error, 1);
-}
+constexpr int kBK = 128;  // one quantisation group per K step
+constexpr uint32_t kSleepLimit = 100000;  // x 10 us sleeps: a wait gives up after ~1 s
+constexpr int kWBytes = 128 * (kBK / 8) * 4;  // 8 KB packed per 128 x 128 tile
+constexpr int kSBytes = 128 * 2;              // 256 B of scales
 
 // Y[m, n] = fp16(sum over splits of partial[s, m, n]); 8 columns per thread.
 __global__ void w4a16_reduce_kernel(const float* __restrict__ part, __half* __restrict__ y, int64_t y_stride,
@@ -317,12 +55,13 @@ __global__ void w4a16_reduce_kernel(const float* __restrict__ part, __half* __re
 }
 
 // W'[k, n] = fp16((q - 8) * scale): the reference dequantisation, for tests.
-// qw is tile-major [N/128][K/128][128][16]; word index -> (n, 8 consecutive k).
+// qw is tile-major [N/128][K/128][4][128][4]; word index -> (n, 8 consecutive k).
 __global__ void w4a16_dequant_kernel(const uint32_t* __restrict__ qw, const __half* __restrict__ scales,
                                      __half* __restrict__ out, int K, int N) {
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // one word = 8 k of one n
   if (idx >= int64_t(N) * (K / 8)) return;
-  const int w16 = int(idx & 15), row = int((idx >> 4) & 127);
+  const int w4 = int(idx & 3), row = int((idx >> 2) & 127), c = int((idx >> 9) & 3);
+  const int w16 = 4 * c + w4;      // word of the row
   const int64_t tile = idx >> 11;  // (n tile, k step)
   const int kt = int(tile % (K / 128)), ntile = int(tile / (K / 128));
   const int n = ntile * 128 + row, kw = kt * 16 + w16;
@@ -336,6 +75,267 @@ __global__ void w4a16_dequant_kernel(const uint32_t* __restrict__ qw, const __ha
     out[int64_t(kw * 8 + 2 * i4) * N + n] = __low2half(h);
     out[int64_t(kw * 8 + 2 * i4 + 1) * N + n] = __high2half(h);
   }
+}
+
+
+// ---------------------------------------------------------------------------
+// GEMM kernel: dequantised weights live in TMEM (tcgen05.mma with A from TMEM).
+//
+// D^T[features, tokens] = W^T[features, K] . X^T: the weight tile is the M=128
+// A operand and sits in tensor memory, the activation tile is the B operand in
+// shared memory (TMA, 128-byte swizzle), the fp32 accumulator is in TMEM.
+//   * Per K step one bulk copy per feature tile brings the packed 8 KB tile
+//     (stored chunk-plane-major, [16-byte chunk][row], so every dequant thread
+//     reads its row's chunks without bank conflicts) into a ring, and one more
+//     brings the step's scales.
+//   * Dequant thread = one output feature (TMEM lane): it expands its 128
+//     int4 values to 64 fp16 pairs in registers and stores them into an A
+//     buffer in TMEM (tcgen05.st): no shared-memory operand tile, no
+//     generic-to-async proxy fence. NA A buffers rotate between the dequant
+//     warps and the MMA thread.
+//   * One thread issues the MMAs (M=128 per feature tile, N = tokens, K=16);
+//     the FT feature tiles share every activation stage.
+//   * Epilogue: the dequant warps read the accumulator back (tcgen05.ld).
+// ---------------------------------------------------------------------------
+constexpr int kMaxNA = 6;          // A buffers in TMEM
+constexpr int kMaxXStages = 10;
+constexpr int kMaxWStages = 10;
+constexpr int kSmem = 216 * 1024;  // dynamic shared memory
+
+struct GemmParams {
+  const uint32_t* qweight;  // tile-major [N/128][K/128][4][128][4]
+  const __half* scales;     // [K/128][N]
+  void* y;                  // fp16 [M, N] (row stride y_stride) or fp32 partials [splits, M, N]
+  int64_t y_stride;
+  int32_t M, N, K;
+  int32_t tn;        // tokens per CTA (MMA N), multiple of 16, <= 256
+  int32_t tn_cols;   // TMEM columns per accumulator (tn rounded up to 32)
+  int32_t na;        // A buffers
+  int32_t x_stages;
+  int32_t w_stages;
+  int32_t k_tiles_per_split;
+};
+
+template <int FT, bool SPLIT>
+__global__ void __launch_bounds__(96 + FT * 256, 1)
+    w4a16_gemm_kernel(const __grid_constant__ CUtensorMap x_map, const GemmParams p) {
+  using namespace sm100;
+  constexpr int kWBytesFT = FT * kWBytes;     // packed weights of one step
+  constexpr int kSBytesFT = FT * kSBytes;     // their scales
+  constexpr int kWStage = kWBytesFT + 1024;   // stage stride (scales after the weights, 1 KB aligned)
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tn = p.tn;
+  const int x_bytes = tn * kBK * 2;
+  const int XS = p.x_stages, WS = p.w_stages, NA = p.na;
+  auto sX = [&](int st) { return base + st * x_bytes; };
+  auto sW = [&](int st) { return base + XS * x_bytes + st * kWStage; };
+
+  __shared__ __align__(8) uint64_t bar_x_full[kMaxXStages], bar_x_empty[kMaxXStages];
+  __shared__ __align__(8) uint64_t bar_w_full[kMaxWStages], bar_w_empty[kMaxWStages];
+  __shared__ __align__(8) uint64_t bar_a_full[kMaxNA], bar_a_empty[kMaxNA], bar_acc;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ftile = blockIdx.x, mblk = blockIdx.y, split = blockIdx.z;
+  const int k_tiles = p.K / kBK;
+  const int kt0 = split * p.k_tiles_per_split;
+  const int nk = max(0, min(k_tiles, kt0 + p.k_tiles_per_split) - kt0);
+  // Every CTA reads the same activation rows: starting the K loop of CTA x at
+  // step x * nk / gridDim.x spreads those reads over the L2 slices (all CTAs
+  // on one 4 KB chunk at once queue behind each other). The order of a CTA's
+  // accumulation is fixed by its index, so results stay deterministic.
+  const int rot = nk > 0 ? int((int64_t(ftile) * nk) / gridDim.x) % nk : 0;
+  auto kt_of = [&](int i) { const int j = i + rot; return kt0 + (j >= nk ? j - nk : j); };
+
+  if (tid == 0) {
+    for (int s = 0; s < XS; ++s) {
+      mbar_init(&bar_x_full[s], 1);
+      mbar_init(&bar_x_empty[s], 1);
+    }
+    for (int s = 0; s < WS; ++s) {
+      mbar_init(&bar_w_full[s], 1);
+      mbar_init(&bar_w_empty[s], FT * 8);  // one arrival per dequant warp
+    }
+    for (int b = 0; b < NA; ++b) {
+      mbar_init(&bar_a_full[b], FT * 8);
+      mbar_init(&bar_a_empty[b], 1);
+    }
+    mbar_init(&bar_acc, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_sh;
+  // TMEM columns: accumulators [FT][tn_cols], then A buffers [NA][FT][64]
+  auto acc_col = [&](int ft) { return uint32_t(ft * p.tn_cols); };
+  auto a_col = [&](int b, int ft) { return uint32_t(FT * p.tn_cols + (b * FT + ft) * 64); };
+
+  if (warp == 0) {
+    // ---------------- producer: step i's activation tile and weight tiles together ----------------
+    // Both rings have the same depth and are refilled in lockstep: the SM's
+    // copy engine serves requests in order, so an activation tile issued
+    // later than the weight stream would wait behind many steps of weights.
+    if (lane == 0) {
+      prefetch_tensormap(&x_map);
+      const int S = XS;  // == WS
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int st = i % S, kt = kt_of(i);
+        if (i >= S) {
+          const uint32_t ph = ((i / S) - 1) & 1;
+          if (!mbar_wait_sleep(&bar_x_empty[st], ph, &abort_flag, kSleepLimit)) break;
+          if (!mbar_wait_sleep(&bar_w_empty[st], ph, &abort_flag, kSleepLimit)) break;
+        }
+        mbar_arrive_expect_tx(&bar_x_full[st], x_bytes);
+        tma_load_3d(sX(st), &x_map, &bar_x_full[st], 0, mblk * tn, kt * 2);
+        // one 8 KB bulk copy per feature tile, then the step's scales
+        mbar_arrive_expect_tx(&bar_w_full[st], kWBytesFT + kSBytesFT);
+#pragma unroll
+        for (int t = 0; t < FT; ++t)
+          bulk_load(sW(st) + t * kWBytes, p.qweight + (int64_t(ftile * FT + t) * k_tiles + kt) * (kWBytes / 4),
+                    kWBytes, &bar_w_full[st]);
+        bulk_load(sW(st) + kWBytesFT, p.scales + int64_t(kt) * p.N + ftile * FT * 128, kSBytesFT, &bar_w_full[st]);
+        issued = i + 1;
+      }
+      if (abort_flag) {  // let the issued copies land before shared memory is released
+        for (int i = max(0, issued - S); i < issued; ++i) {
+          uint32_t n = 0;
+          while (!mbar_try_wait(&bar_x_full[i % S], (i / S) & 1) && ++n < kSleepLimit) {}
+          n = 0;
+          while (!mbar_try_wait(&bar_w_full[i % S], (i / S) & 1) && ++n < kSleepLimit) {}
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    // The issue loop is the throughput limit at small N (an MMA takes ~45
+    // cycles at N <= 64), so descriptors are built once: the K-slice kk of
+    // stage sx starts (kk / 4) * tn * 128 + (kk % 4) * 32 bytes after the
+    // stage, i.e. that many 16-byte units added to the descriptor's address
+    // field (bits 0-13, which these offsets never carry out of).
+    if (lane == 0) {
+      const uint32_t idesc = f16_idesc(0, 0, 0, 128, uint32_t(tn));
+      const uint64_t xdesc0 = sw128_desc(smem_addr(sX(0)), 16, 1024);
+      const uint32_t x_stage_units = uint32_t(x_bytes >> 4), kblk_units = uint32_t(tn * 8);
+      for (int i = 0; i < nk; ++i) {
+        const int sx = i % XS, b = i % NA;
+        if (!mbar_wait_sleep(&bar_x_full[sx], (i / XS) & 1, &abort_flag, kSleepLimit)) break;
+        if (!mbar_wait_sleep(&bar_a_full[b], (i / NA) & 1, &abort_flag, kSleepLimit)) break;
+        tc_fence_after();
+        const uint64_t xd0 = xdesc0 + uint64_t(sx * x_stage_units);
+        const uint32_t ta0 = tbase + a_col(b, 0);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t xd = xd0 + uint64_t((kk / 4) * kblk_units + (kk % 4) * 2);
+#pragma unroll
+          for (int ft = 0; ft < FT; ++ft)
+            mma_ts(tbase + acc_col(ft), ta0 + ft * 64 + kk * 8, xd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&bar_x_empty[sx]);
+        mma_commit(&bar_a_empty[b]);
+      }
+      mma_commit(&bar_acc);
+    }
+  } else if (warp >= 3) {  // (warp 2 has no role)
+    // ---------------- dequantisation: thread = (output feature, half of the 128 k) ----------------
+    // Dequant warp dw: group g = dw / 4 -> feature tile g % FT, k half g / FT;
+    // the 4 warps of a group cover the 4 TMEM lane quarters (warp & 3).
+    const int dw = (tid - 96) >> 5;
+    const int g = dw >> 2;
+    const int ft = g % FT, kh = g / FT;
+    const int quarter = warp & 3;          // TMEM lanes this warp may access
+    const int f = quarter * 32 + lane;     // feature row inside the tile (= TMEM lane)
+    const int n = (ftile * FT + ft) * 128 + f;
+    // int4 -> fp16 without shifts for half of the pairs: OR-ing 0x6400 onto a
+    // nibble at bits 0-3 gives 1024 + q, at bits 4-7 gives 1024 + 16 q; then
+    // q - 8 = x - 1032 or x / 16 - 72, both exact in fp16.
+    const __half2 c1032 = __floats2half2_rn(1032.f, 1032.f);
+    const __half2 c16 = __floats2half2_rn(0.0625f, 0.0625f), c72 = __floats2half2_rn(-72.f, -72.f);
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int st = i % WS, b = i % NA;
+      ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar_w_full[st], (i / WS) & 1, &abort_flag, kSleepLimit));
+      if (!ok) break;
+      // stage layout: [tile][chunk c][row][16 B] then scales [tile][row] fp16;
+      // this thread's k half is chunks 2 kh, 2 kh + 1 (words 8 kh .. 8 kh + 7)
+      const uint32_t sw = smem_addr(sW(st));
+      uint32_t words[8];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint4 v = lds128(sw + ft * kWBytes + (2 * kh + c) * (128 * 16) + f * 16);
+        words[4 * c] = v.x; words[4 * c + 1] = v.y; words[4 * c + 2] = v.z; words[4 * c + 3] = v.w;
+      }
+      const __half sh = __ushort_as_half(lds16(sw + kWBytesFT + (ft * 128 + f) * 2));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_w_empty[st]);  // words and scale are in registers
+      const __half2 s2 = __halves2half2(sh, sh);
+      if (i >= NA) {
+        ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar_a_empty[b], ((i / NA) - 1) & 1, &abort_flag, kSleepLimit));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      uint32_t o[32];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        // word w holds k = 8 w' .. 8 w' + 7 as the pairs (0,1) bits 0-3|16-19,
+        // (2,3) bits 4-7|20-23, (4,5) and (6,7) the same 8 bits higher
+        const uint32_t lo = words[w], hi = words[w] >> 8;
+        const uint32_t b0 = (lo & 0x000F000Fu) | 0x64006400u, b1 = (lo & 0x00F000F0u) | 0x64006400u;
+        const uint32_t b2 = (hi & 0x000F000Fu) | 0x64006400u, b3 = (hi & 0x00F000F0u) | 0x64006400u;
+        const __half2 q0 = __hsub2(*reinterpret_cast<const __half2*>(&b0), c1032);
+        const __half2 q1 = __hfma2(*reinterpret_cast<const __half2*>(&b1), c16, c72);
+        const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&b2), c1032);
+        const __half2 q3 = __hfma2(*reinterpret_cast<const __half2*>(&b3), c16, c72);
+        const __half2 h0 = __hmul2(q0, s2), h1 = __hmul2(q1, s2), h2 = __hmul2(q2, s2), h3 = __hmul2(q3, s2);
+        o[4 * w] = *reinterpret_cast<const uint32_t*>(&h0);
+        o[4 * w + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+        o[4 * w + 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        o[4 * w + 3] = *reinterpret_cast<const uint32_t*>(&h3);
+      }
+      tmem_st32(tbase + (uint32_t(quarter * 32) << 16) + a_col(b, ft) + 32 * kh, o);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_a_full[b]);
+    }
+    // ---------------- epilogue: TMEM lane = feature n, column = token ----------------
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar_acc, 0, &abort_flag, kSleepLimit));
+    if (ok) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c4 = kh; c4 * 32 < tn; c4 += 2) {  // the two k-half warps split the token columns
+        uint32_t acc[32];
+        tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft) + c4 * 32, acc);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int m = mblk * tn + c4 * 32 + c;
+          if (c4 * 32 + c >= tn || m >= p.M) break;
+          if constexpr (SPLIT)
+            reinterpret_cast<float*>(p.y)[(int64_t(split) * p.M + m) * p.N + n] = __uint_as_float(acc[c]);
+          else
+            reinterpret_cast<__half*>(p.y)[int64_t(m) * p.y_stride + n] = __float2half_rn(__uint_as_float(acc[c]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+  if (tid == 0 && abort_flag) atomicExch(&g_w4a16_error, 1);
 }
 
 }  // namespace
@@ -382,23 +382,84 @@ int sm_count() {
 
 }  // namespace
 
-// Split-K factor for an (M, N, K) problem: enough CTAs for every SM when the
-// makespan estimate over the candidate split counts.
+// Tile shape: FT feature tiles of 128 x tn tokens per CTA.
+struct GemmShape {
+  int ft, tn;
+};
+GemmShape gemm_shape(int M, int N) {
+  const bool ft2 = N % 256 == 0;
+  if (M <= 128) return {ft2 ? 2 : 1, ((M + 15) / 16) * 16};
+  if (M <= 256) return {1, ((M + 15) / 16) * 16};
+  return ft2 ? GemmShape{2, 128} : GemmShape{1, 256};
+}
+
+// Split-K factor for the GEMM kernel: minimise (waves of CTAs) x (K steps per
+// CTA + pipeline fill of ~4 steps), plus the reduce pass when split.
 int w4a16_auto_splits(int M, int N, int K) {
-  const int m_tile = M <= 64 ? ((M + 15) / 16) * 16 : kBM;
-  const int tiles = ((M + m_tile - 1) / m_tile) * ((N + kBN - 1) / kBN);
+  const GemmShape sh = gemm_shape(M, N);
+  const int tiles = ((M + sh.tn - 1) / sh.tn) * (N / (128 * sh.ft));
   const int k_tiles = K / kBK;
   const int sms = sm_count();
-  // minimise (waves of CTAs) x (K steps per CTA + fixed cost of ~3 steps)
   int best = 1;
   double best_cost = 1e30;
   for (int s = 1; s <= k_tiles && s <= 64; s *= 2) {
     const int per = (k_tiles + s - 1) / s;
     const int ctas = tiles * ((k_tiles + per - 1) / per);
-    const double cost = double((ctas + sms - 1) / sms) * (per + 3) + (s > 1 ? 2.0 : 0.0);
+    const double cost = double((ctas + sms - 1) / sms) * (per + 4) + (s > 1 ? 2.0 : 0.0);
     if (cost < best_cost) { best_cost = cost; best = s; }
   }
   return best;
+}
+
+// Launches the GEMM (and the split-K reduce). Arguments are validated by the caller.
+int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t st) {
+  const GemmShape sh = gemm_shape(a.M, a.N);
+  CUtensorMap xm;
+  if (!make_x_map(&xm, a.x, a.K, a.M, a.x_stride, sh.tn)) return QA_ERR_ALIGN;
+  GemmParams p;
+  p.qweight = reinterpret_cast<const uint32_t*>(a.qweight);
+  p.scales = reinterpret_cast<const __half*>(a.scales);
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.tn = sh.tn;
+  p.tn_cols = ((sh.tn + 31) / 32) * 32;
+  p.na = (512 - sh.ft * p.tn_cols) / (sh.ft * 64);
+  if (p.na > kMaxNA) p.na = kMaxNA;
+  if (p.na < 2) return QA_ERR_UNSUPPORTED;
+  const int w_stage = sh.ft * kWBytes + 1024;
+  const int x_bytes = sh.tn * kBK * 2;
+  // one ring depth for both (the producer refills them in lockstep)
+  int stages = (kSmem - 1024) / (x_bytes + w_stage);
+  if (stages > kMaxXStages) stages = kMaxXStages;
+  if (stages < 2) return QA_ERR_UNSUPPORTED;
+  p.x_stages = p.w_stages = stages;
+  p.k_tiles_per_split = per;
+  const dim3 grid{unsigned(a.N / (128 * sh.ft)), unsigned((a.M + sh.tn - 1) / sh.tn), unsigned(splits)};
+  const bool split = splits > 1;
+  auto kern = sh.ft == 2 ? (split ? w4a16_gemm_kernel<2, true> : w4a16_gemm_kernel<2, false>)
+                         : (split ? w4a16_gemm_kernel<1, true> : w4a16_gemm_kernel<1, false>);
+  static bool attr[4] = {false, false, false, false};
+  const int ai = (sh.ft - 1) * 2 + split;
+  if (!attr[ai]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+      return QA_ERR_LAUNCH;
+    attr[ai] = true;
+  }
+  const int threads = 96 + sh.ft * 256;
+  if (split) {
+    p.y = a.workspace;
+    p.y_stride = a.N;
+    kern<<<grid, threads, kSmem, st>>>(xm, p);
+    const int64_t vec = int64_t(a.M) * a.N / 8;
+    w4a16_reduce_kernel<<<unsigned((vec + 255) / 256), 256, 0, st>>>(
+        a.workspace, reinterpret_cast<__half*>(a.y), a.y_stride, a.M, a.N, splits);
+  } else {
+    p.y = a.y;
+    p.y_stride = a.y_stride;
+    kern<<<grid, threads, kSmem, st>>>(xm, p);
+  }
+  return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
 
 int w4a16_read_clear_error() {
@@ -440,52 +501,7 @@ extern "C" int qa_w4a16_gemm(const qa_w4a16_args* args, void* stream) {
   splits = (k_tiles + per - 1) / per;  // no empty split
   if (splits > 1 && (a.workspace == nullptr || (reinterpret_cast<uintptr_t>(a.workspace) & 15u)))
     return QA_ERR_INVALID;
-  const bool swap = a.M <= 64;
-  const int m_pad = swap ? ((a.M + 15) / 16) * 16 : kBM;
-  CUtensorMap xm;
-  if (!make_x_map(&xm, a.x, a.K, a.M, a.x_stride, m_pad)) return QA_ERR_ALIGN;
-  W4Params p;
-  p.qweight = reinterpret_cast<const uint32_t*>(a.qweight);
-  p.scales = reinterpret_cast<const __half*>(a.scales);
-  p.m_pad = m_pad;
-  {
-    // shared memory: dequantised B tiles (32 KB each) + weight ring + activation ring
-    const int x_bytes = m_pad * kBK * 2;
-    p.b_bufs = 2;
-    p.w_stages = swap ? 8 : 4;
-    const int avail = kSmem - 1024 - p.b_bufs * kBBytes - p.w_stages * kWStageBytes;
-    p.x_stages = avail / x_bytes < kMaxStages ? avail / x_bytes : kMaxStages;
-    if (p.x_stages < 2) return QA_ERR_UNSUPPORTED;
-  }
-  p.M = a.M;
-  p.N = a.N;
-  p.K = a.K;
-  p.k_tiles_per_split = per;
-  p.split = splits;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const dim3 grid{unsigned((a.M + m_pad - 1) / m_pad), unsigned((a.N + kBN - 1) / kBN), unsigned(splits)};
-  static bool attr[4] = {false, false, false, false};
-  const bool split = splits > 1;
-  auto kern = split ? (swap ? w4a16_gemm_kernel<true, true> : w4a16_gemm_kernel<true, false>)
-                    : (swap ? w4a16_gemm_kernel<false, true> : w4a16_gemm_kernel<false, false>);
-  if (!attr[split * 2 + swap]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
-      return QA_ERR_LAUNCH;
-    attr[split * 2 + swap] = true;
-  }
-  if (split) {
-    p.y = a.workspace;
-    p.y_stride = a.N;
-    kern<<<grid, kThreads, kSmem, st>>>(xm, p);
-    const int64_t vec = int64_t(a.M) * a.N / 8;
-    w4a16_reduce_kernel<<<unsigned((vec + 255) / 256), 256, 0, st>>>(
-        a.workspace, reinterpret_cast<__half*>(a.y), a.y_stride, a.M, a.N, splits);
-  } else {
-    p.y = a.y;
-    p.y_stride = a.y_stride;
-    kern<<<grid, kThreads, kSmem, st>>>(xm, p);
-  }
-  return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
+  return w4a16_gemm_launch(a, splits, per, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int qa_w4a16_dequant(const int32_t* qweight, const void* scales, void* out, int32_t K, int32_t N,

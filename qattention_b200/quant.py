@@ -16,10 +16,13 @@ calibration step, out of scope for random-init weights):
 * Dequantisation: ``w = fp16((q - 8) * scale)`` (exact product, one rounding).
 
 Packing (this library's layout, chosen for the GEMM kernel): ``qweight`` is
-int32 ``[N // 128, K // 128, 128, 16]`` — tile-major, so the 128 output
+int32 ``[N // 128, K // 128, 4, 128, 4]`` — tile-major, so the 128 output
 columns x 128 k of one GEMM step are one contiguous 8 KB block that a single
-bulk copy fetches. Inside a tile, row j is output column 128 * tile + j and
-word w holds k = 8 w .. 8 w + 7 of that step with the nibbles interleaved:
+bulk copy fetches, stored chunk-plane-major inside the tile: index
+``[tile_n, tile_k, c, j, w]`` is output column 128 * tile_n + j, word 4 c + w
+of its row, which holds k = 8 (4 c + w) .. + 7 of that step (the 16-byte
+chunks of one plane c are consecutive rows, so the GEMM's per-row reads from
+shared memory are bank-conflict free). The nibbles of a word are interleaved:
 k % 8 = 2i sits in nibble i and k % 8 = 2i + 1 in nibble i + 4 (i = 0..3),
 so ``(word >> 4i) & 0x000F000F`` yields the consecutive pair (2i, 2i+1) as the
 two halves of a 32-bit lane. ``scales`` is fp16 ``[K // 128, N]``. No
@@ -37,7 +40,7 @@ NIBBLE_SHIFT = (0, 16, 4, 20, 8, 24, 12, 28)
 
 def quantize_w4a16(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Quantise a ``[K, N]`` weight (Y = X @ W) to
-    ``(qweight [N/128, K/128, 128, 16] int32, scales [K/128, N] fp16)``.
+    ``(qweight [N/128, K/128, 4, 128, 4] int32, scales [K/128, N] fp16)``.
 
     Runs with torch ops on W's device (CPU or CUDA); the result is identical on both.
     """
@@ -54,15 +57,15 @@ def quantize_w4a16(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=W.device)
     words = (qt.to(torch.int64) << shifts).sum(dim=-1)          # 0 .. 2^32-1
     words = torch.where(words < 2**31, words, words - 2**32).to(torch.int32)  # [N, K/8]
-    qweight = words.view(N // 128, 128, K // 128, 16).permute(0, 2, 1, 3).contiguous()
+    qweight = words.view(N // 128, 128, K // 128, 4, 4).permute(0, 2, 3, 1, 4).contiguous()
     return qweight, scales.contiguous()
 
 
 def unpack_int4(qweight: torch.Tensor) -> torch.Tensor:
-    """Tile-major ``[N/128, K/128, 128, 16]`` int32 -> ``[K, N]`` int32 values in 0..15 (host helper)."""
+    """Tile-major ``[N/128, K/128, 4, 128, 4]`` int32 -> ``[K, N]`` int32 values in 0..15 (host helper)."""
     NT, KT = qweight.shape[:2]
     N, K8 = NT * 128, KT * 16
-    w = qweight.permute(0, 2, 1, 3).reshape(N, K8).to(torch.int64) & 0xFFFFFFFF
+    w = qweight.permute(0, 3, 1, 2, 4).reshape(N, K8).to(torch.int64) & 0xFFFFFFFF
     shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=qweight.device)
     vals = (w[..., None] >> shifts) & 0xF                         # [N, K/8, 8]
     return vals.reshape(N, K8 * 8).t().to(torch.int32).contiguous()
@@ -72,7 +75,7 @@ def w4a16_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
                  splits: int = 0, out: torch.Tensor = None) -> torch.Tensor:
     """``x @ dequant(qweight, scales)`` on the B200 tensor cores (fp16 in/out, fp32 accumulate).
 
-    x: ``[..., K]`` fp16 CUDA (unit stride along K); qweight ``[N, K/8]`` int32,
+    x: ``[..., K]`` fp16 CUDA (unit stride along K); qweight ``[N/128, K/128, 4, 128, 4]`` int32,
     scales ``[K/128, N]`` fp16 (see :func:`quantize_w4a16`). ``splits`` = K split
     across CTAs (0 = automatic); a split-K run uses a temporary fp32 workspace.
     """

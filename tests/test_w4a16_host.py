@@ -12,7 +12,7 @@ def test_quantiser_matches_oracle_bit_exact():
     W[:128, 3] = 0.0  # an all-zero group
     qw, sc = quant.quantize_w4a16(W)
     q_ref, s_ref = wo.quantize(W.numpy())
-    assert qw.dtype == torch.int32 and qw.shape == (1, 4, 128, 16)
+    assert qw.dtype == torch.int32 and qw.shape == (1, 4, 4, 128, 4)
     assert sc.dtype == torch.float16 and sc.shape == (4, 128)
     assert np.array_equal(sc.numpy().view(np.uint16), s_ref.view(np.uint16))
     assert np.array_equal(qw.numpy(), wo.pack(q_ref))
