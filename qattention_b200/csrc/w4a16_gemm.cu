@@ -157,10 +157,10 @@ __global__ void __launch_bounds__(96 + FT * 256, 1)
     }
     for (int s = 0; s < WS; ++s) {
       mbar_init(&bar_w_full[s], 1);
-      mbar_init(&bar_w_empty[s], FT * 8);  // one arrival per dequant warp
+      mbar_init(&bar_w_empty[s], FT * 4);  // one arrival per warp of the step's dequant group
     }
     for (int b = 0; b < NA; ++b) {
-      mbar_init(&bar_a_full[b], FT * 8);
+      mbar_init(&bar_a_full[b], FT * 4);
       mbar_init(&bar_a_empty[b], 1);
     }
     mbar_init(&bar_acc, 1);
@@ -246,12 +246,13 @@ __global__ void __launch_bounds__(96 + FT * 256, 1)
       mma_commit(&bar_acc);
     }
   } else if (warp >= 3) {  // (warp 2 has no role)
-    // ---------------- dequantisation: thread = (output feature, half of the 128 k) ----------------
-    // Dequant warp dw: group g = dw / 4 -> feature tile g % FT, k half g / FT;
-    // the 4 warps of a group cover the 4 TMEM lane quarters (warp & 3).
+    // ---------------- dequantisation: thread = output feature, group = every other K step ----------------
+    // Dequant warp dw: group gr = dw / (4 FT) takes the steps i with i % 2 == gr
+    // (two steps in flight); inside a group, warp w -> feature tile (w / 4) % FT,
+    // and the 4 warps of a tile cover the 4 TMEM lane quarters (warp & 3).
     const int dw = (tid - 96) >> 5;
-    const int g = dw >> 2;
-    const int ft = g % FT, kh = g / FT;
+    const int gr = dw / (4 * FT);
+    const int ft = (dw >> 2) % FT;
     const int quarter = warp & 3;          // TMEM lanes this warp may access
     const int f = quarter * 32 + lane;     // feature row inside the tile (= TMEM lane)
     const int n = (ftile * FT + ft) * 128 + f;
@@ -261,17 +262,16 @@ __global__ void __launch_bounds__(96 + FT * 256, 1)
     const __half2 c1032 = __floats2half2_rn(1032.f, 1032.f);
     const __half2 c16 = __floats2half2_rn(0.0625f, 0.0625f), c72 = __floats2half2_rn(-72.f, -72.f);
     bool ok = true;
-    for (int i = 0; i < nk; ++i) {
+    for (int i = gr; i < nk; i += 2) {
       const int st = i % WS, b = i % NA;
       ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar_w_full[st], (i / WS) & 1, &abort_flag, kSleepLimit));
       if (!ok) break;
-      // stage layout: [tile][chunk c][row][16 B] then scales [tile][row] fp16;
-      // this thread's k half is chunks 2 kh, 2 kh + 1 (words 8 kh .. 8 kh + 7)
+      // stage layout: [tile][chunk c][row][16 B] then scales [tile][row] fp16
       const uint32_t sw = smem_addr(sW(st));
-      uint32_t words[8];
+      uint32_t words[16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint4 v = lds128(sw + ft * kWBytes + (2 * kh + c) * (128 * 16) + f * 16);
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = lds128(sw + ft * kWBytes + c * (128 * 16) + f * 16);
         words[4 * c] = v.x; words[4 * c + 1] = v.y; words[4 * c + 2] = v.z; words[4 * c + 3] = v.w;
       }
       const __half sh = __ushort_as_half(lds16(sw + kWBytesFT + (ft * 128 + f) * 2));
@@ -283,25 +283,28 @@ __global__ void __launch_bounds__(96 + FT * 256, 1)
         if (!ok) break;
         tc_fence_after();
       }
-      uint32_t o[32];
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        // word w holds k = 8 w' .. 8 w' + 7 as the pairs (0,1) bits 0-3|16-19,
-        // (2,3) bits 4-7|20-23, (4,5) and (6,7) the same 8 bits higher
-        const uint32_t lo = words[w], hi = words[w] >> 8;
-        const uint32_t b0 = (lo & 0x000F000Fu) | 0x64006400u, b1 = (lo & 0x00F000F0u) | 0x64006400u;
-        const uint32_t b2 = (hi & 0x000F000Fu) | 0x64006400u, b3 = (hi & 0x00F000F0u) | 0x64006400u;
-        const __half2 q0 = __hsub2(*reinterpret_cast<const __half2*>(&b0), c1032);
-        const __half2 q1 = __hfma2(*reinterpret_cast<const __half2*>(&b1), c16, c72);
-        const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&b2), c1032);
-        const __half2 q3 = __hfma2(*reinterpret_cast<const __half2*>(&b3), c16, c72);
-        const __half2 h0 = __hmul2(q0, s2), h1 = __hmul2(q1, s2), h2 = __hmul2(q2, s2), h3 = __hmul2(q3, s2);
-        o[4 * w] = *reinterpret_cast<const uint32_t*>(&h0);
-        o[4 * w + 1] = *reinterpret_cast<const uint32_t*>(&h1);
-        o[4 * w + 2] = *reinterpret_cast<const uint32_t*>(&h2);
-        o[4 * w + 3] = *reinterpret_cast<const uint32_t*>(&h3);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t o[32];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          // word w holds 8 consecutive k as the pairs (0,1) bits 0-3|16-19,
+          // (2,3) bits 4-7|20-23, (4,5) and (6,7) the same 8 bits higher
+          const uint32_t lo = words[8 * h + w], hi = lo >> 8;
+          const uint32_t b0 = (lo & 0x000F000Fu) | 0x64006400u, b1 = (lo & 0x00F000F0u) | 0x64006400u;
+          const uint32_t b2 = (hi & 0x000F000Fu) | 0x64006400u, b3 = (hi & 0x00F000F0u) | 0x64006400u;
+          const __half2 q0 = __hsub2(*reinterpret_cast<const __half2*>(&b0), c1032);
+          const __half2 q1 = __hfma2(*reinterpret_cast<const __half2*>(&b1), c16, c72);
+          const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&b2), c1032);
+          const __half2 q3 = __hfma2(*reinterpret_cast<const __half2*>(&b3), c16, c72);
+          const __half2 h0 = __hmul2(q0, s2), h1 = __hmul2(q1, s2), h2 = __hmul2(q2, s2), h3 = __hmul2(q3, s2);
+          o[4 * w] = *reinterpret_cast<const uint32_t*>(&h0);
+          o[4 * w + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+          o[4 * w + 2] = *reinterpret_cast<const uint32_t*>(&h2);
+          o[4 * w + 3] = *reinterpret_cast<const uint32_t*>(&h3);
+        }
+        tmem_st32(tbase + (uint32_t(quarter * 32) << 16) + a_col(b, ft) + 32 * h, o);
       }
-      tmem_st32(tbase + (uint32_t(quarter * 32) << 16) + a_col(b, ft) + 32 * kh, o);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -312,7 +315,7 @@ __global__ void __launch_bounds__(96 + FT * 256, 1)
     if (ok) {
       tc_fence_after();
 #pragma unroll 1
-      for (int c4 = kh; c4 * 32 < tn; c4 += 2) {  // the two k-half warps split the token columns
+      for (int c4 = gr; c4 * 32 < tn; c4 += 2) {  // the two groups split the token columns
         uint32_t acc[32];
         tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft) + c4 * 32, acc);
         tmem_wait_ld();
