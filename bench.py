@@ -16,6 +16,16 @@ all-gather of per-rank checksums afterwards.
 
 ``--impl reference`` times the reference's CPU path for this operator (padded
 masked SDPA, restated in oracle/, all host threads) on a bounded sample.
+
+Secondary arms (one JSON line each, N=1; used for the profiles of the other
+hot-path kernels, not the headline):
+``--kernel prefix``  BASELINE config 4's shared-prefix pass (B=16, L=10240 prefix
+                     keys, 341 tree queries, GQA 32/8, D=128): TFLOP/s against
+                     the measured bf16 tensor peak.
+``--kernel w4a16``   the seven W4A16 linears of one Llama-3.1-8B decoder layer
+                     (config 5's architecture, random-init int4 weights) at
+                     M = 16, 64, 1023 and 8184 tokens; value = weight-stream
+                     GB/s at M = 64 (HBM-bound regime), the sweep in ``sweep``.
 """
 from __future__ import annotations
 
@@ -357,6 +367,128 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def _timed_graphs(graphs, steps, warmup, dev):
+    """Replays the captured graphs round-robin; returns ms per replay (CUDA events)."""
+    for i in range(warmup):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize(dev)
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for i in range(steps):
+        graphs[i % len(graphs)].replay()
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / steps
+
+
+def _capture(fn, n, dev):
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for i in range(n):
+            fn(i)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    graphs = []
+    for i in range(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn(i)
+        graphs.append(g)
+    return graphs
+
+
+def _tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def run_prefix(args):
+    """Shared-prefix pass of config 4 (tcgen05 kernel), TFLOP/s."""
+    from qattention_b200 import ragged_attn as ra
+    dev = torch.device("cuda", 0)
+    B, L, N, Hq, Hkv, D = 16, 10240, 341, 32, 8, 128
+    g = torch.Generator().manual_seed(4)
+    Q = torch.randn(B, N, Hq, D, generator=g).half().to(dev)
+    K = torch.randn(B, L, Hkv, D, generator=g).half().to(dev)
+    V = torch.randn(B, L, Hkv, D, generator=g).half().to(dev)
+    graphs = _capture(lambda i: ra.prefix_attention_with_lse(Q, K, V), 1, dev)
+    clocks = ClockSampler(0)
+    clocks.start()
+    clocks.mark("t0")
+    ms = _timed_graphs(graphs, args.steps, args.warmup, dev)
+    clocks.mark("t1")
+    clocks.stop()
+    flops = 4.0 * B * Hq * N * L * D
+    tf = flops / (ms * 1e-3) / 1e12
+    peak, kind = _tensor_peak()
+    print(json.dumps({
+        "metric": "prefix pass TFLOP/s", "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "f16",
+        "data": "synthetic", "config": {"workload": "C4 prefix pass: B=16, L=10240 prefix keys, N=341 tree "
+                                        "queries, GQA 32/8, D=128, fp16", "l2": "K/V 671 MB > L2"},
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                     "peak_kind": kind, "flops_per_launch": flops, "kernel": "prefix_attn_kernel (qa_prefix_attn)"},
+        "gpu_launches": args.steps, "clocks": clocks.summary()}), flush=True)
+
+
+LLAMA_LINEARS = [  # (name, K, N) of one Llama-3.1-8B decoder layer, Y = X W with W [K, N]
+    ("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
+    ("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)]
+
+
+def run_w4a16(args):
+    """One decoder layer's W4A16 linears (random-init int4 weights) at several M."""
+    from qattention_b200 import quant
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(5)
+    layer = []
+    for _, K, N in LLAMA_LINEARS:
+        qw, sc = quant.quantize_w4a16(torch.randn(K, N, generator=g) * 0.02)
+        layer.append((qw.to(dev), sc.to(dev), K, N))
+    wbytes = sum(qw.numel() * 4 + sc.numel() * 2 for qw, sc, _, _ in layer)
+    copies = max(2, -(-3 * L2_BYTES // wbytes))
+    layers = [layer] + [[(qw.clone(), sc.clone(), K, N) for qw, sc, K, N in layer] for _ in range(copies - 1)]
+    clocks = ClockSampler(0)
+    clocks.start()
+    clocks.mark("t0")
+    sweep = {}
+    for M in (16, 64, 1023, 8184):
+        xs = {K: torch.randn(M, K, device=dev).half() for K in (4096, 14336)}
+        ys = [torch.empty(M, N, dtype=torch.float16, device=dev) for _, _, _, N in layer]
+
+        def step(i, M=M, xs=xs, ys=ys):
+            for j, (qw, sc, K, N) in enumerate(layers[i % copies]):
+                quant.w4a16_linear(xs[K], qw, sc, out=ys[j])
+
+        graphs = _capture(step, copies, dev)
+        steps = max(copies, min(args.steps, 200 if M <= 1023 else 40))
+        ms = _timed_graphs(graphs, steps, args.warmup, dev)
+        flops = sum(2.0 * M * K * N for _, _, K, N in layer)
+        sweep[str(M)] = {"us_per_layer": ms * 1e3, "weight_gbs": wbytes / (ms * 1e-3) / 1e9,
+                         "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_layer": len(layer)}
+        del graphs
+    clocks.mark("t1")
+    clocks.stop()
+    hb, hkind = _peaks()
+    tp, tkind = _tensor_peak()
+    v = sweep["64"]["weight_gbs"]
+    print(json.dumps({
+        "metric": "W4A16 weight-stream GB/s (M=64)", "value": v, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sweep["64"]["us_per_layer"] * 1e-3,
+        "higher_is_better": True, "dtype": "int4 x f16 -> f32 acc", "data": "synthetic (random-init weights)",
+        "config": {"workload": "Llama-3.1-8B decoder layer, 7 W4A16 linears (218.1 M weights, group 128)",
+                   "l2": f"{copies} rotating weight copies (> 3x L2)"},
+        "roofline": {"bound": "hbm", "achieved": v, "peak": hb, "unit": "GB/s", "frac": v / hb, "peak_kind": hkind,
+                     "bytes_per_layer": wbytes, "kernel": "w4a16_gemm_kernel (qa_w4a16_gemm)"},
+        "large_m_roofline": {"bound": "tensor", "M": 8184, "achieved": sweep["8184"]["tflops"], "peak": tp,
+                             "unit": "TFLOP/s", "frac": sweep["8184"]["tflops"] / tp, "peak_kind": tkind},
+        "sweep": sweep, "clocks": clocks.summary()}), flush=True)
+
+
 def _finish():
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         import torch.distributed as dist
@@ -373,11 +505,16 @@ def main():
     ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--kernel", default="ancestor", choices=["ancestor", "prefix", "w4a16"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.kernel == "prefix":
+        run_prefix(args)
+    elif args.kernel == "w4a16":
+        run_w4a16(args)
     else:
         run_ours(args)
     _finish()
