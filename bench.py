@@ -22,7 +22,8 @@ hot-path kernels, not the headline):
 ``--kernel prefix``  BASELINE config 4's shared-prefix pass (B=16, L=10240 prefix
                      keys, 341 tree queries, GQA 32/8, D=128): TFLOP/s against
                      the measured bf16 tensor peak.
-``--kernel w4a16``   the seven W4A16 linears of one Llama-3.1-8B decoder layer
+``--kernel w4a16``   the W4A16 linears of one Llama-3.1-8B decoder layer (q/k/v
+                     and gate/up fused along N: 4 GEMMs)
                      (config 5's architecture, random-init int4 weights) at
                      M = 16, 64, 1023 and 8184 tokens; value = weight-stream
                      GB/s at M = 64 (HBM-bound regime), the sweep in ``sweep``.
@@ -435,14 +436,15 @@ def run_prefix(args):
         "gpu_launches": args.steps, "clocks": clocks.summary()}), flush=True)
 
 
-LLAMA_LINEARS = [  # (name, K, N) of one Llama-3.1-8B decoder layer, Y = X W with W [K, N]
-    ("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
-    ("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)]
+# (name, K, N) of one Llama-3.1-8B decoder layer, Y = X W with W [K, N]; q/k/v
+# and gate/up are fused along N as serving stacks load them (same weights, 4 GEMMs)
+LLAMA_LINEARS = [("qkv", 4096, 6144), ("o", 4096, 4096), ("gate_up", 4096, 28672), ("down", 14336, 4096)]
 
 
 def run_w4a16(args):
     """One decoder layer's W4A16 linears (random-init int4 weights) at several M."""
-    from qattention_b200 import quant
+    import ctypes
+    from qattention_b200 import _lib, quant
     dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(5)
     layer = []
@@ -468,8 +470,13 @@ def run_w4a16(args):
         steps = max(copies, min(args.steps, 200 if M <= 1023 else 40))
         ms = _timed_graphs(graphs, steps, args.warmup, dev)
         flops = sum(2.0 * M * K * N for _, _, K, N in layer)
+        launches = 0
+        for _, _, K, N in layer:  # one GEMM, plus the split-K reduce when the plan splits K
+            sp, wb = ctypes.c_int32(), ctypes.c_int64()
+            _lib.check(_lib.lib().qa_w4a16_plan(M, N, K, ctypes.byref(sp), ctypes.byref(wb)), "qa_w4a16_plan")
+            launches += 1 + (sp.value > 1)
         sweep[str(M)] = {"us_per_layer": ms * 1e3, "weight_gbs": wbytes / (ms * 1e-3) / 1e9,
-                         "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_layer": len(layer)}
+                         "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_layer": launches}
         del graphs
     clocks.mark("t1")
     clocks.stop()
@@ -480,7 +487,8 @@ def run_w4a16(args):
         "metric": "W4A16 weight-stream GB/s (M=64)", "value": v, "unit": "GB/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sweep["64"]["us_per_layer"] * 1e-3,
         "higher_is_better": True, "dtype": "int4 x f16 -> f32 acc", "data": "synthetic (random-init weights)",
-        "config": {"workload": "Llama-3.1-8B decoder layer, 7 W4A16 linears (218.1 M weights, group 128)",
+        "config": {"workload": "Llama-3.1-8B decoder layer W4A16 linears, qkv and gate_up fused "
+                                "(4 GEMMs, 218.1 M weights, group 128)",
                    "l2": f"{copies} rotating weight copies (> 3x L2)"},
         "roofline": {"bound": "hbm", "achieved": v, "peak": hb, "unit": "GB/s", "frac": v / hb, "peak_kind": hkind,
                      "bytes_per_layer": wbytes, "kernel": "w4a16_gemm_kernel (qa_w4a16_gemm)"},

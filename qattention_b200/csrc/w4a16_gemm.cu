@@ -33,25 +33,41 @@ constexpr uint32_t kSleepLimit = 100000;  // x 10 us sleeps: a wait gives up aft
 constexpr int kWBytes = 128 * (kBK / 8) * 4;  // 8 KB packed per 128 x 128 tile
 constexpr int kSBytes = 128 * 2;              // 256 B of scales
 
-// Y[m, n] = fp16(sum over splits of partial[s, m, n]); 8 columns per thread.
-__global__ void w4a16_reduce_kernel(const float* __restrict__ part, __half* __restrict__ y, int64_t y_stride,
-                                    int M, int N, int splits) {
-  const int64_t idx = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
-  if (idx >= int64_t(M) * N) return;
-  const int m = int(idx / N), n = int(idx % N);
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < splits; ++s) {
-    const float4* src = reinterpret_cast<const float4*>(part + (int64_t(s) * M + m) * N + n);
-    const float4 a = src[0], b = src[1];
-    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-    acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+// Y[m, n] = fp16(sum over splits of partial[s, m, n]), summed in split order
+// (deterministic). Block = 32 float4 column chunks x 8 split groups: thread
+// (c, g) adds splits g, g + 8, ... of its 4 outputs, then the 8 group sums are
+// added in g order through shared memory. Many blocks even when M x N is small.
+__global__ void __launch_bounds__(256) w4a16_reduce_kernel(const float* __restrict__ part, __half* __restrict__ y,
+                                                          int64_t y_stride, int M, int N, int splits) {
+  __shared__ float4 sums[8][32];
+  const int c = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int64_t q = int64_t(blockIdx.x) * 32 + c;  // float4 chunk of the M x N output
+  const int64_t MN4 = int64_t(M) * N / 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (q < MN4) {
+    const float4* src = reinterpret_cast<const float4*>(part) + q;
+#pragma unroll 4
+    for (int s = g; s < splits; s += 8) {
+      const float4 v = __ldg(src + int64_t(s) * MN4);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
   }
-  uint32_t h[4];
-  for (int c = 0; c < 4; ++c) {
-    __half2 v = __floats2half2_rn(acc[2 * c], acc[2 * c + 1]);
-    h[c] = *reinterpret_cast<uint32_t*>(&v);
+  sums[g][c] = acc;
+  __syncthreads();
+  if (g == 0 && q < MN4) {
+#pragma unroll
+    for (int k = 1; k < 8; ++k) {
+      const float4 v = sums[k][c];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const int64_t idx = q * 4;
+    const int m = int(idx / N), n = int(idx % N);
+    const __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&lo);
+    o.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(y + int64_t(m) * y_stride + n) = o;
   }
-  *reinterpret_cast<uint4*>(y + int64_t(m) * y_stride + n) = make_uint4(h[0], h[1], h[2], h[3]);
 }
 
 // W'[k, n] = fp16((q - 8) * scale): the reference dequantisation, for tests.
@@ -100,7 +116,8 @@ __global__ void w4a16_dequant_kernel(const uint32_t* __restrict__ qw, const __ha
 constexpr int kMaxNA = 6;          // A buffers in TMEM
 constexpr int kMaxXStages = 10;
 constexpr int kMaxWStages = 10;
-constexpr int kSmem = 216 * 1024;  // dynamic shared memory
+constexpr int kSmem = 216 * 1024;   // dynamic shared memory, one CTA per SM
+constexpr int kSmem2 = 108 * 1024;  // two CTAs per SM
 
 struct GemmParams {
   const uint32_t* qweight;  // tile-major [N/128][K/128][4][128][4]
@@ -116,8 +133,12 @@ struct GemmParams {
   int32_t k_tiles_per_split;
 };
 
-template <int FT, bool SPLIT>
-__global__ void __launch_bounds__(96 + FT * 256, 1)
+// CPS = CTAs resident per SM (1 or 2): with 2, each CTA takes half of the
+// TMEM columns and of the shared memory, and two independent pipelines
+// interleave on the SM (the per-step latency chain of one pipeline caps its
+// weight stream well below the SM's share of HBM bandwidth).
+template <int FT, bool SPLIT, int CPS>
+__global__ void __launch_bounds__(96 + FT * 256, CPS)
     w4a16_gemm_kernel(const __grid_constant__ CUtensorMap x_map, const GemmParams p) {
   using namespace sm100;
   constexpr int kWBytesFT = FT * kWBytes;     // packed weights of one step
@@ -168,7 +189,7 @@ __global__ void __launch_bounds__(96 + FT * 256, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_sh, 512);
+    tmem_alloc(&tmem_base_sh, 512 / CPS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -336,7 +357,7 @@ __global__ void __launch_bounds__(96 + FT * 256, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tbase, 512);
+    tmem_dealloc(tbase, 512 / CPS);
   }
   if (tid == 0 && abort_flag) atomicExch(&g_w4a16_error, 1);
 }
@@ -387,13 +408,14 @@ int sm_count() {
 
 // Tile shape: FT feature tiles of 128 x tn tokens per CTA.
 struct GemmShape {
-  int ft, tn;
+  int ft, tn, cps;  // feature tiles per CTA, tokens per CTA, CTAs per SM
 };
 GemmShape gemm_shape(int M, int N) {
   const bool ft2 = N % 256 == 0;
-  if (M <= 128) return {ft2 ? 2 : 1, ((M + 15) / 16) * 16};
-  if (M <= 256) return {1, ((M + 15) / 16) * 16};
-  return ft2 ? GemmShape{2, 128} : GemmShape{1, 256};
+  if (M <= 64) return {1, ((M + 15) / 16) * 16, 2};
+  if (M <= 128) return {ft2 ? 2 : 1, ((M + 15) / 16) * 16, 1};
+  if (M <= 256) return {1, ((M + 15) / 16) * 16, 1};
+  return ft2 ? GemmShape{2, 128, 1} : GemmShape{1, 256, 1};
 }
 
 // Split-K factor for the GEMM kernel: minimise (waves of CTAs) x (K steps per
@@ -402,13 +424,16 @@ int w4a16_auto_splits(int M, int N, int K) {
   const GemmShape sh = gemm_shape(M, N);
   const int tiles = ((M + sh.tn - 1) / sh.tn) * (N / (128 * sh.ft));
   const int k_tiles = K / kBK;
-  const int sms = sm_count();
+  const int sms = sm_count() * sh.cps;  // resident CTA slots
   int best = 1;
   double best_cost = 1e30;
   for (int s = 1; s <= k_tiles && s <= 64; s *= 2) {
     const int per = (k_tiles + s - 1) / s;
     const int ctas = tiles * ((k_tiles + per - 1) / per);
-    const double cost = double((ctas + sms - 1) / sms) * (per + 4) + (s > 1 ? 2.0 : 0.0);
+    // unit = one K step (~1.2 us); the reduce reads splits x M x N fp32 partials
+    // (~3 TB/s) and costs a launch (~2 us)
+    const double reduce = s > 1 ? 2.0 + double(s) * M * N * 4 / 3.0e12 / 1.2e-6 : 0.0;
+    const double cost = double((ctas + sms - 1) / sms) * (per + 4) + reduce;
     if (cost < best_cost) { best_cost = cost; best = s; }
   }
   return best;
@@ -427,25 +452,27 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   p.K = a.K;
   p.tn = sh.tn;
   p.tn_cols = ((sh.tn + 31) / 32) * 32;
-  p.na = (512 - sh.ft * p.tn_cols) / (sh.ft * 64);
+  p.na = (512 / sh.cps - sh.ft * p.tn_cols) / (sh.ft * 64);
   if (p.na > kMaxNA) p.na = kMaxNA;
   if (p.na < 2) return QA_ERR_UNSUPPORTED;
   const int w_stage = sh.ft * kWBytes + 1024;
   const int x_bytes = sh.tn * kBK * 2;
   // one ring depth for both (the producer refills them in lockstep)
-  int stages = (kSmem - 1024) / (x_bytes + w_stage);
+  const int smem = sh.cps == 2 ? kSmem2 : kSmem;
+  int stages = (smem - 1024) / (x_bytes + w_stage);
   if (stages > kMaxXStages) stages = kMaxXStages;
   if (stages < 2) return QA_ERR_UNSUPPORTED;
   p.x_stages = p.w_stages = stages;
   p.k_tiles_per_split = per;
   const dim3 grid{unsigned(a.N / (128 * sh.ft)), unsigned((a.M + sh.tn - 1) / sh.tn), unsigned(splits)};
   const bool split = splits > 1;
-  auto kern = sh.ft == 2 ? (split ? w4a16_gemm_kernel<2, true> : w4a16_gemm_kernel<2, false>)
-                         : (split ? w4a16_gemm_kernel<1, true> : w4a16_gemm_kernel<1, false>);
-  static bool attr[4] = {false, false, false, false};
-  const int ai = (sh.ft - 1) * 2 + split;
+  auto kern = sh.cps == 2 ? (split ? w4a16_gemm_kernel<1, true, 2> : w4a16_gemm_kernel<1, false, 2>)
+            : sh.ft == 2  ? (split ? w4a16_gemm_kernel<2, true, 1> : w4a16_gemm_kernel<2, false, 1>)
+                          : (split ? w4a16_gemm_kernel<1, true, 1> : w4a16_gemm_kernel<1, false, 1>);
+  static bool attr[6] = {false, false, false, false, false, false};
+  const int ai = (sh.cps == 2 ? 4 : (sh.ft - 1) * 2) + split;
   if (!attr[ai]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return QA_ERR_LAUNCH;
     attr[ai] = true;
   }
@@ -453,14 +480,14 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   if (split) {
     p.y = a.workspace;
     p.y_stride = a.N;
-    kern<<<grid, threads, kSmem, st>>>(xm, p);
-    const int64_t vec = int64_t(a.M) * a.N / 8;
-    w4a16_reduce_kernel<<<unsigned((vec + 255) / 256), 256, 0, st>>>(
+    kern<<<grid, threads, smem, st>>>(xm, p);
+    const int64_t vec = int64_t(a.M) * a.N / 4;
+    w4a16_reduce_kernel<<<unsigned((vec + 31) / 32), 256, 0, st>>>(
         a.workspace, reinterpret_cast<__half*>(a.y), a.y_stride, a.M, a.N, splits);
   } else {
     p.y = a.y;
     p.y_stride = a.y_stride;
-    kern<<<grid, threads, kSmem, st>>>(xm, p);
+    kern<<<grid, threads, smem, st>>>(xm, p);
   }
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
