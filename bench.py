@@ -22,6 +22,10 @@ hot-path kernels, not the headline):
 ``--kernel prefix``  BASELINE config 4's shared-prefix pass (B=16, L=10240 prefix
                      keys, 341 tree queries, GQA 32/8, D=128): TFLOP/s against
                      the measured bf16 tensor peak.
+``--kernel verify``  config 5: the W4A16 tree-verify step of random-init
+                     Llama-3.1-8B (32 layers) on B=8 sequences (2048-token prefix
+                     + binary depth-9 tree), tokens/s; under torchrun the 8
+                     sequences are split over the ranks (strong scaling).
 ``--kernel w4a16``   the W4A16 linears of one Llama-3.1-8B decoder layer (q/k/v
                      and gate/up fused along N: 4 GEMMs)
                      (config 5's architecture, random-init int4 weights) at
@@ -499,6 +503,73 @@ def run_w4a16(args):
         "sweep": sweep, "clocks": clocks.summary()}), flush=True)
 
 
+def run_verify(args):
+    """Config 5: W4A16 tree-verify step of random-init Llama-3.1-8B, tokens/s (strong scaling over ranks)."""
+    from qattention_b200 import verify as vf
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    B_all, L, b, d = 8, 2048, 2, 9
+    if B_all % ws:
+        raise SystemExit("config 5 shards 8 sequences: use 1, 2, 4 or 8 GPUs")
+    B = B_all // ws
+    N = _num_nodes(b, d)
+    cfg = vf.LlamaConfig()
+    if args.verify_layers:
+        cfg.layers = args.verify_layers
+    model = vf.VerifyModel(cfg, dev, seed=7)
+    cache = model.new_cache(B, L, N, seed=8 + rank)
+    g = torch.Generator().manual_seed(9 + rank)
+    tok_host = torch.randint(0, cfg.vocab, (B, N), generator=g).pin_memory()
+    tokens = tok_host.to(dev)
+    steps = max(1, min(args.steps, 10))
+    for _ in range(max(args.warmup, 2)):
+        model.step(tokens, cache, L, b, d)
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    if rank == 0:
+        clocks.start()
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(ws)
+    torch.cuda.synchronize(dev)
+    clocks.mark("t0")
+    e0.record(cur)
+    for _ in range(steps):
+        model.step(tokens, cache, L, b, d)
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    clocks.mark("t1")
+    ms = _max_over_ranks(e0.elapsed_time(e1) / steps, ws)
+    if rank == 0:
+        clocks.stop()
+    # end to end: tokens H2D from pinned memory, the step, argmax tokens D2H
+    out_host = torch.empty(B * N, dtype=torch.int64).pin_memory()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(ws)
+    f0.record(cur)
+    for _ in range(steps):
+        t = tok_host.to(dev, non_blocking=True)
+        out_host.copy_(model.step(t, cache, L, b, d).argmax(-1), non_blocking=True)
+    f1.record(cur)
+    torch.cuda.synchronize(dev)
+    e2e_ms = _max_over_ranks(f0.elapsed_time(f1) / steps, ws)
+    if rank != 0:
+        return
+    tokens_total = B_all * N
+    print(json.dumps({
+        "metric": "W4A16 verify-step tokens/s", "value": tokens_total / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": ws, "steps": steps, "warmup": max(args.warmup, 2), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 weights x f16 activations, f32 accumulate", "data": "synthetic (random-init weights, random tokens)",
+        "config": {"workload": f"C5: random-init Llama-3.1-8B architecture ({cfg.layers} layers), W4A16 linears "
+                               "(qkv and gate_up fused), fp16 LM head; B=8 sequences x (2048-token cached prefix "
+                               "+ binary depth-9 tree, 1023 tokens) = 8184 verify tokens per step",
+                   "sequences_per_gpu": B, "parallelism": f"sequences sharded over {ws} GPU(s), no collective"},
+        "e2e": {"value": tokens_total / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": B * N * 8, "d2h_bytes_per_step": B * N * 8},
+        "clocks": clocks.summary()}), flush=True)
+
+
 def _finish():
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         import torch.distributed as dist
@@ -515,7 +586,8 @@ def main():
     ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--kernel", default="ancestor", choices=["ancestor", "prefix", "w4a16"])
+    ap.add_argument("--kernel", default="ancestor", choices=["ancestor", "prefix", "w4a16", "verify"])
+    ap.add_argument("--verify-layers", type=int, default=0, help="override the layer count (tests only)")
     ap.add_argument("--w4-m", default="16,64,1023,8184", help="token counts of the w4a16 arm")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -526,6 +598,8 @@ def main():
         run_prefix(args)
     elif args.kernel == "w4a16":
         run_w4a16(args)
+    elif args.kernel == "verify":
+        run_verify(args)
     else:
         run_ours(args)
     _finish()

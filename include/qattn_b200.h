@@ -204,6 +204,34 @@ QA_API int qa_w4a16_dequant(const int32_t* qweight, const void* scales, void* ou
                             void* stream);
 
 /*
+ * Elementwise steps of the W4A16 verify step (the Llama
+ * decoder-layer code the reference runs around its attention,
+ * scripts/w4a16_e2e.py:1393-1431). fp16 tensors, fp32 arithmetic, 16-byte
+ * aligned, contiguous rows.
+ *
+ * qa_add_rmsnorm: for each of M rows of `hidden` elements: h += delta (when
+ * delta is not NULL, h updated in place), out = fp16(h * rsqrt(mean(h^2) + eps))
+ * * w (HF LlamaRMSNorm order).
+ */
+QA_API int qa_add_rmsnorm(void* h, const void* delta, const void* w, void* out, int32_t M, int32_t hidden,
+                          float eps, void* stream);
+
+/*
+ * qa_rope_qkv: qkv = [M, (hq + 2 hkv) * head_dim] fused projection of M tokens
+ * (n_per_seq tokens per sequence, sequence b = row / n_per_seq). Rotate-half
+ * RoPE at position pos[row] with frequencies inv_freq[head_dim/2] (fp32) is
+ * applied to the q heads in place; the rotated k heads and the v heads are
+ * written to k_cache / v_cache ([B, hkv, S, head_dim] with element strides
+ * kv_stride_b, kv_stride_h; token offset kv_offset + row % n_per_seq).
+ */
+QA_API int qa_rope_qkv(void* qkv, const int32_t* pos, const float* inv_freq, void* k_cache, void* v_cache,
+                       int32_t M, int32_t n_per_seq, int32_t hq, int32_t hkv, int32_t head_dim,
+                       int64_t kv_stride_b, int64_t kv_stride_h, int32_t kv_offset, void* stream);
+
+/* qa_silu_mul: out[M, F] = silu(gate_up[:, :F]) * gate_up[:, F:] (F % 8 == 0). */
+QA_API int qa_silu_mul(const void* gate_up, void* out, int32_t M, int32_t F, void* stream);
+
+/*
  * Reads and clears the device error flag that the tensor-core kernels set when
  * one of their bounded pipeline waits times out (a kernel that hits it stops,
  * frees its resources and leaves its outputs incomplete). Synchronising call.

@@ -18,6 +18,9 @@ QA_DTYPE_BF16 = 1
 
 # Every symbol the header declares; tests check the library exports all of them.
 EXPORTED = (
+    "qa_add_rmsnorm",
+    "qa_rope_qkv",
+    "qa_silu_mul",
     "qa_ancestor_attn",
     "qa_lse_merge",
     "qa_prefix_attn",
@@ -113,6 +116,13 @@ def lib() -> ctypes.CDLL:
         L.qa_w4a16_plan.restype = c_int
         L.qa_w4a16_dequant.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_void_p]
         L.qa_w4a16_dequant.restype = c_int
+        L.qa_add_rmsnorm.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]
+        L.qa_add_rmsnorm.restype = c_int
+        L.qa_rope_qkv.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                  c_int32, c_int32, c_int64, c_int64, c_int32, c_void_p]
+        L.qa_rope_qkv.restype = c_int
+        L.qa_silu_mul.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_void_p]
+        L.qa_silu_mul.restype = c_int
         L.qa_status_string.argtypes = [c_int]
         L.qa_status_string.restype = c_char_p
         L.qa_version.argtypes = []
