@@ -420,6 +420,9 @@ GemmShape gemm_shape(int M, int N) {
   if (M <= 64) return {1, ((M + 15) / 16) * 16, 2};
   if (M <= 128) return {ft2 ? 2 : 1, ((M + 15) / 16) * 16, 1};
   if (M <= 256) return {1, ((M + 15) / 16) * 16, 1};
+  // up to ~2K tokens two CTAs per SM overlap one CTA's prologue/epilogue with
+  // the other's main loop (+8-19 % at M = 1023); beyond that one wide CTA
+  if (M <= 2048) return {1, 128, 2};
   return ft2 ? GemmShape{2, 128, 1} : GemmShape{1, 256, 1};
 }
 
