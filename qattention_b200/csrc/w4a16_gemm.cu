@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
 
   __shared__ __align__(8) uint64_t bar_x_full[kMaxXStages], bar_x_empty[kMaxXStages];
   __shared__ __align__(8) uint64_t bar_w_full[kMaxWStages], bar_w_empty[kMaxWStages];
-  __shared__ __align__(8) uint64_t bar_a_full[kMaxNA], bar_a_empty[kMaxNA], bar_acc;
+  __shared__ __align__(8) uint64_t bar_a_empty[kMaxNA], bar_acc, bar_step[kMaxXStages];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
@@ -172,18 +172,21 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
   auto kt_of = [&](int i) { const int j = i + rot; return kt0 + (j >= nk ? j - nk : j); };
 
   if (tid == 0) {
+    // bar_step: one arrival per dequant warp of the step's group, each made
+    // after the warp saw the step's activation tile land (bar_x_full) and
+    // stored its A rows; the MMA thread waits on it alone, once per step (a
+    // wait costs a few hundred cycles in this kernel, and the MMA thread is its
+    // critical path)
     for (int s = 0; s < XS; ++s) {
       mbar_init(&bar_x_full[s], 1);
       mbar_init(&bar_x_empty[s], 1);
+      mbar_init(&bar_step[s], FT * 4);
     }
     for (int s = 0; s < WS; ++s) {
       mbar_init(&bar_w_full[s], 1);
       mbar_init(&bar_w_empty[s], FT * 4);  // one arrival per warp of the step's dequant group
     }
-    for (int b = 0; b < NA; ++b) {
-      mbar_init(&bar_a_full[b], FT * 4);
-      mbar_init(&bar_a_empty[b], 1);
-    }
+    for (int b = 0; b < NA; ++b) mbar_init(&bar_a_empty[b], 1);
     mbar_init(&bar_acc, 1);
     abort_flag = 0;
     fence_barrier_init();
@@ -249,8 +252,7 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
       const uint32_t x_stage_units = uint32_t(x_bytes >> 4), kblk_units = uint32_t(tn * 8);
       for (int i = 0; i < nk; ++i) {
         const int sx = i % XS, b = i % NA;
-        if (!mbar_wait_sleep(&bar_x_full[sx], (i / XS) & 1, &abort_flag, kSleepLimit)) break;
-        if (!mbar_wait_sleep(&bar_a_full[b], (i / NA) & 1, &abort_flag, kSleepLimit)) break;
+        if (!mbar_wait_sleep(&bar_step[sx], (i / XS) & 1, &abort_flag, kSleepLimit)) break;
         tc_fence_after();
         const uint64_t xd0 = xdesc0 + uint64_t(sx * x_stage_units);
         const uint32_t ta0 = tbase + a_col(b, 0);
@@ -333,8 +335,10 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
       }
       tmem_wait_st();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_a_full[b]);
+      // the step's activation tile (issued with its weights) has landed as well
+      ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar_x_full[i % XS], (i / XS) & 1, &abort_flag, kSleepLimit));
+      if (!ok) break;
+      if (lane == 0) mbar_arrive(&bar_step[i % XS]);  // A rows of step i are in TMEM
     }
     // ---------------- epilogue: TMEM lane = feature n, column = token ----------------
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar_acc, 0, &abort_flag, kSleepLimit));
