@@ -288,16 +288,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_s = f16_idesc(FMT, 0, 0, kBM, kBN);
       const uint32_t idesc_o = f16_idesc(FMT, 0, 1, kBM, D);
-      const uint32_t q_addr = smem_addr(sQ);
+      // Descriptors are built once and advanced by constants: the 64-bit
+      // bit-field assembly per MMA costs about as much issue time as the MMA.
+      // Offsets go into the 16-byte-unit address field (bits 0-13), which
+      // shared-memory offsets never carry out of.
+      constexpr uint32_t kStageUnits = uint32_t(2 * PfxSmem<D>::KV_BYTES) >> 4;
+      const uint64_t q_desc = sw128_desc(smem_addr(sQ), 16, 1024);
+      const uint64_t k_desc0 = sw128_desc(smem_addr(sK(0)), 16, 1024);
+      const uint64_t v_desc0 = sw128_desc(smem_addr(sV(0)), kBN * 128, 1024);
       auto issue_pv = [&](int i) -> bool {
         if (!mbar_wait(&bar_p_full[i & 1], (i >> 1) & 1, &abort_flag, kWaitLimit)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_addr(sV(i % kStages));
+        const uint64_t v_desc = v_desc0 + uint64_t((i % kStages) * kStageUnits);
+        const uint32_t p_tmem = tbase + (i & 1) * kBN;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, kBN * 128, 1024);
-          mma_ts(tmem_o, tbase + (i & 1) * kBN + kk * 8, bdesc, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts(tmem_o, p_tmem + kk * 8, v_desc + uint64_t(kk * 128), idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bar_o_done);
         mma_commit(&bar_kv_empty[i % kStages]);
         return true;
@@ -307,13 +313,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % kStages;
         if (!mbar_wait(&bar_kv_full[st], (j / kStages) & 1, &abort_flag, kWaitLimit)) break;
         tc_fence_after();
-        const uint32_t k_addr = smem_addr(sK(st));
+        const uint64_t k_desc = k_desc0 + uint64_t(st * kStageUnits);
+        const uint32_t s_tmem = tbase + (j & 1) * kBN;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t adesc = sw128_desc(q_addr + (kk / 4) * kBM * 128 + (kk % 4) * 32, 16, 1024);
-          const uint64_t bdesc = sw128_desc(k_addr + (kk / 4) * kBN * 128 + (kk % 4) * 32, 16, 1024);
-          mma_ss(tbase + (j & 1) * kBN, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(s_tmem, q_desc + uint64_t((kk / 4) * kBM * 8 + (kk % 4) * 2),
+                 k_desc + uint64_t((kk / 4) * kBN * 8 + (kk % 4) * 2), idesc_s, kk > 0 ? 1u : 0u);
         mma_commit(&bar_s_full[j & 1]);
         if (j >= 1) ok = issue_pv(j - 1);
       }
