@@ -128,6 +128,7 @@ struct GemmParams {
   int32_t tn;        // tokens per CTA (MMA N), multiple of 16, <= 256
   int32_t tn_cols;   // TMEM columns per accumulator (tn rounded up to 32)
   int32_t na;        // A buffers
+  int32_t dual;      // two MMA threads (even / odd K steps), one accumulator each
   int32_t x_stages;
   int32_t w_stages;
   int32_t k_tiles_per_split;
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
       mbar_init(&bar_w_empty[s], FT * 4);  // one arrival per warp of the step's dequant group
     }
     for (int b = 0; b < NA; ++b) mbar_init(&bar_a_empty[b], 1);
-    mbar_init(&bar_acc, 1);
+    mbar_init(&bar_acc, p.dual ? 2 : 1);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -199,9 +200,10 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = tmem_base_sh;
-  // TMEM columns: accumulators [FT][tn_cols], then A buffers [NA][FT][64]
-  auto acc_col = [&](int ft) { return uint32_t(ft * p.tn_cols); };
-  auto a_col = [&](int b, int ft) { return uint32_t(FT * p.tn_cols + (b * FT + ft) * 64); };
+  // TMEM columns: accumulators [1 or 2 MMA threads][FT][tn_cols], then A buffers [NA][FT][64]
+  const int nacc = p.dual ? 2 : 1;
+  auto acc_col = [&](int ft, int par) { return uint32_t((par * FT + ft) * p.tn_cols); };
+  auto a_col = [&](int b, int ft) { return uint32_t(nacc * FT * p.tn_cols + (b * FT + ft) * 64); };
 
   if (warp == 0) {
     // ---------------- producer: step i's activation tile and weight tiles together ----------------
@@ -239,18 +241,23 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
         }
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 || (warp == 2 && p.dual)) {
+    // ---------------- MMA issuer(s) ----------------
+    // With `dual`, warp 1 issues the even K steps into accumulator 0 and warp 2
+    // the odd ones into accumulator 1, so one thread's barrier waits overlap the
+    // other's MMAs (a single issuing thread is this kernel's critical path at
+    // small M); the epilogue adds the two accumulators in a fixed order.
     // The issue loop is the throughput limit at small N (an MMA takes ~45
     // cycles at N <= 64), so descriptors are built once: the K-slice kk of
     // stage sx starts (kk / 4) * tn * 128 + (kk % 4) * 32 bytes after the
     // stage, i.e. that many 16-byte units added to the descriptor's address
     // field (bits 0-13, which these offsets never carry out of).
     if (lane == 0) {
+      const int par = warp - 1, stride = p.dual ? 2 : 1;
       const uint32_t idesc = f16_idesc(0, 0, 0, 128, uint32_t(tn));
       const uint64_t xdesc0 = sw128_desc(smem_addr(sX(0)), 16, 1024);
       const uint32_t x_stage_units = uint32_t(x_bytes >> 4), kblk_units = uint32_t(tn * 8);
-      for (int i = 0; i < nk; ++i) {
+      for (int i = par; i < nk; i += stride) {
         const int sx = i % XS, b = i % NA;
         if (!mbar_wait_sleep(&bar_step[sx], (i / XS) & 1, &abort_flag, kSleepLimit)) break;
         tc_fence_after();
@@ -261,14 +268,14 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
           const uint64_t xd = xd0 + uint64_t((kk / 4) * kblk_units + (kk % 4) * 2);
 #pragma unroll
           for (int ft = 0; ft < FT; ++ft)
-            mma_ts(tbase + acc_col(ft), ta0 + ft * 64 + kk * 8, xd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tbase + acc_col(ft, par), ta0 + ft * 64 + kk * 8, xd, idesc, (i >= stride || kk > 0) ? 1u : 0u);
         }
         mma_commit(&bar_x_empty[sx]);
         mma_commit(&bar_a_empty[b]);
       }
       mma_commit(&bar_acc);
     }
-  } else if (warp >= 3) {  // (warp 2 has no role)
+  } else if (warp >= 3) {  // (warp 2 issues MMAs only in dual mode)
     // ---------------- dequantisation: thread = output feature, group = every other K step ----------------
     // Dequant warp dw: group gr = dw / (4 FT) takes the steps i with i % 2 == gr
     // (two steps in flight); inside a group, warp w -> feature tile (w / 4) % FT,
@@ -347,7 +354,14 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
 #pragma unroll 1
       for (int c4 = gr; c4 * 32 < tn; c4 += 2) {  // the two groups split the token columns
         uint32_t acc[32];
-        tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft) + c4 * 32, acc);
+        tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft, 0) + c4 * 32, acc);
+        if (p.dual && nk > 1) {  // odd steps' accumulator (empty when there is one step)
+          uint32_t acc1[32];
+          tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft, 1) + c4 * 32, acc1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) acc[c] = __float_as_uint(__uint_as_float(acc[c]) + __uint_as_float(acc1[c]));
+        }
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -464,7 +478,9 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   p.K = a.K;
   p.tn = sh.tn;
   p.tn_cols = ((sh.tn + 31) / 32) * 32;
-  p.na = (512 / sh.cps - sh.ft * p.tn_cols) / (sh.ft * 64);
+  // two MMA threads (one accumulator each) when their accumulators and >= 2 A buffers fit
+  p.dual = (512 / sh.cps - 2 * sh.ft * p.tn_cols) / (sh.ft * 64) >= 2 ? 1 : 0;
+  p.na = (512 / sh.cps - (p.dual ? 2 : 1) * sh.ft * p.tn_cols) / (sh.ft * 64);
   if (p.na > kMaxNA) p.na = kMaxNA;
   if (p.na < 2) return QA_ERR_UNSUPPORTED;
   const int w_stage = sh.ft * kWBytes + 1024;
