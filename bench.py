@@ -26,6 +26,8 @@ hot-path kernels, not the headline):
                      Llama-3.1-8B (32 layers) on B=8 sequences (2048-token prefix
                      + binary depth-9 tree), tokens/s; under torchrun the 8
                      sequences are split over the ranks (strong scaling).
+``--kernel hybrid``  config 4 whole: prefix pass + ancestor pass with the LSE
+                     merge fused (``tree_verify_attention``), µs per call.
 ``--kernel w4a16``   the W4A16 linears of one Llama-3.1-8B decoder layer (q/k/v
                      and gate/up fused along N: 4 GEMMs)
                      (config 5's architecture, random-init int4 weights) at
@@ -442,6 +444,35 @@ def run_prefix(args):
 
 # (name, K, N) of one Llama-3.1-8B decoder layer, Y = X W with W [K, N]; q/k/v
 # and gate/up are fused along N as serving stacks load them (same weights, 4 GEMMs)
+def run_hybrid(args):
+    """Config 4 whole verify attention: tcgen05 prefix pass + ancestor pass with the LSE merge fused."""
+    from qattention_b200 import ragged_attn as ra
+    dev = torch.device("cuda", 0)
+    B, L, b, d, Hq, Hkv, D = 16, 10240, 4, 4, 32, 8, 128
+    N = _num_nodes(b, d)
+    g = torch.Generator().manual_seed(6)
+    Q = torch.randn(B, Hq, N, D, generator=g).half().to(dev)
+    K = torch.randn(B, Hkv, L + N, D, generator=g).half().to(dev)
+    V = torch.randn(B, Hkv, L + N, D, generator=g).half().to(dev)
+    graphs = _capture(lambda i: ra.tree_verify_attention(Q, K, V, b, d), 1, dev)
+    clocks = ClockSampler(0)
+    clocks.start()
+    clocks.mark("t0")
+    ms = _timed_graphs(graphs, args.steps, args.warmup, dev)
+    clocks.mark("t1")
+    clocks.stop()
+    prefix_flops = 4.0 * B * Hq * N * L * D
+    print(json.dumps({
+        "metric": "tree-verify attention us (prefix + tree, merged)", "value": ms * 1e3, "unit": "us",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+        "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "C4: B=16, L=10240 cached prefix + complete 4-ary depth-4 tree (N=341), "
+                               "GQA 32/8, D=128; ragged_attention tree_verify_attention (KV cache layout "
+                               "[B, Hkv, L+N, D], no repeat_kv)", "l2": "K/V 2.1 GB > L2"},
+        "prefix_tflops": prefix_flops / (ms * 1e-3) / 1e12,
+        "gpu_launches": args.steps * 2, "clocks": clocks.summary()}), flush=True)
+
+
 LLAMA_LINEARS = [("qkv", 4096, 6144), ("o", 4096, 4096), ("gate_up", 4096, 28672), ("down", 14336, 4096)]
 
 
@@ -586,7 +617,7 @@ def main():
     ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--kernel", default="ancestor", choices=["ancestor", "prefix", "w4a16", "verify"])
+    ap.add_argument("--kernel", default="ancestor", choices=["ancestor", "prefix", "hybrid", "w4a16", "verify"])
     ap.add_argument("--verify-layers", type=int, default=0, help="override the layer count (tests only)")
     ap.add_argument("--w4-m", default="16,64,1023,8184", help="token counts of the w4a16 arm")
     args = ap.parse_args()
@@ -596,6 +627,8 @@ def main():
         run_reference(args)
     elif args.kernel == "prefix":
         run_prefix(args)
+    elif args.kernel == "hybrid":
+        run_hybrid(args)
     elif args.kernel == "w4a16":
         run_w4a16(args)
     elif args.kernel == "verify":

@@ -261,7 +261,15 @@ def prefix_attention_with_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
     the prefix phase of the reference's ``_ragged_tree_attn``
     (scripts/w4a16_e2e.py:1236-1253), without materialising ``repeat_kv``.
     """
-    _check_qkv(Q.flatten(0, 1), K.flatten(0, 1), V.flatten(0, 1))
+    # checked in place: flattening permuted cache views would copy them
+    assert Q.dtype in _SUPPORTED and Q.dtype == K.dtype == V.dtype, (
+        f"Inputs must be fp16 or bf16 (got {Q.dtype})"
+    )
+    for name, t in (("Q", Q), ("K", K), ("V", V)):
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor: this library has no CPU path")
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be [batch, tokens, heads, head_dim], got shape {tuple(t.shape)}")
     B, N, Hq, D = Q.shape
     L, Hkv = K.shape[1], K.shape[2]
     O = torch.empty(B, N, Hq, D, dtype=Q.dtype, device=Q.device)
