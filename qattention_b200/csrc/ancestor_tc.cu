@@ -1,28 +1,30 @@
-// Ancestor-walk attention, complete-tree mode, level-at-a-time on tensor cores.
+// Ancestor-walk attention, complete-tree mode, on tensor cores (mma.sync).
 //
 // Same result as the scalar walk in ancestor_attn.cu (and as the reference's
 // _ragged_attn_sparse_kernel(_lse), src/ragged_attn.py:267-496), organised so
 // that per-query overhead disappears:
-//   * A warp owns 16 consecutive BFS queries of one (sequence, head). At walk
-//     level s their ancestors are a contiguous node range of at most 16 rows
-//     (see ancestor_plan.cuh), already staged in shared memory by the CTA.
-//   * S = Q (16 x D) . K_level^T (D x 16) with mma.sync m16n8k16 (fp32
-//     accumulate); each query row keeps the one column that is its step-s
-//     ancestor (or none when its walk has ended), so the softmax sees exactly
-//     the reference's key set.
-//   * O += P . V_level with P the one-hot row of that weight (fp16, or bf16
-//     split into hi + lo parts so the weight keeps ~16 bits), again one
-//     m16n8k16 per 8 output columns. The softmax reference maximum moves only
-//     when a score exceeds it by 2^8 (lazy rescale; exact result).
-//   * Tensor cores here only cut instruction count (the whole kernel is a
-//     gather with ~2.8 flop per HBM byte): one level of 16 queries costs ~70
-//     warp instructions instead of ~650 for a per-query scalar walk.
-//   * Shared rows use a 16-byte-chunk XOR swizzle (chunk ^ (row & 7)) so the
-//     ldmatrix row reads are bank-conflict free; the output tile is written
-//     back through the same shared region as 16-byte row vectors.
+//   * Work item = (sequence, tile of 64 consecutive BFS queries, query head);
+//     a persistent grid (one CTA per resident slot) takes equal contiguous
+//     ranges of the items, tile-major, and plans each tile once for all of its
+//     heads.
+//   * Plan: at walk level s the ancestors of a contiguous query range are a
+//     contiguous node range (ancestor_plan.cuh); the tile's levels merge into
+//     windows of K/V rows that are staged in shared memory once per head.
+//   * A warp owns 16 queries; their keys over all levels form one key list
+//     (<= 128 columns). S = Q . K_list^T runs as mma.sync m16n8k16 (fp32
+//     accumulate) with S kept in registers; a per-thread bitmask (built once
+//     per tile) keeps exactly each row's walk keys, so the softmax (exact, row
+//     max over the walk) sees the reference's key set. P is normalised, rounded
+//     to fp16 (bf16: hi + lo split) and reused from the S registers as the A
+//     operand of O = P . V_list.
+//   * Tensor cores here only cut instruction count: the pass is a gather bound
+//     by HBM bandwidth (~2.8 flop per byte).
+//   * Shared rows use a 16-byte-chunk XOR swizzle (chunk ^ (row & 7)), unrolled
+//     into the ldmatrix/stmatrix addresses, so row reads are bank-conflict
+//     free; the output tile leaves through stmatrix and 16-byte streaming
+//     stores.
 // Used when every walk level of a tile fits in shared memory (always true for
 // b >= 2; chains up to depth ~300), for head_dim 64, 128 and 256.
-#include <atomic>
 #include "ancestor_plan.cuh"
 
 namespace qa {

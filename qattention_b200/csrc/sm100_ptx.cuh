@@ -1,4 +1,5 @@
-// Thin wrappers over the sm_100a PTX used by the prefix pass: mbarriers with
+// Thin wrappers over the sm_100a PTX used by the prefix pass and the W4A16
+// GEMM: mbarriers with
 // bounded waits, TMA tile loads (global -> this CTA's shared memory only),
 // and the 5th-generation tensor-core instructions (tcgen05: TMEM allocation,
 // MMA with TMEM accumulators, commit, TMEM loads/stores, fences).
