@@ -25,6 +25,8 @@
 //     stores.
 // Used when every walk level of a tile fits in shared memory (always true for
 // b >= 2; chains up to depth ~300), for head_dim 64, 128 and 256.
+#include <atomic>
+
 #include "ancestor_plan.cuh"
 
 namespace qa {
