@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   __shared__ int w_levels[kWarps], w_nwin[kWarps];
   __shared__ int kslot[kWarps][kTcMaxKeys];       // staged K/V row of each key column
 
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a following GEMM may stage
   const qa_ancestor_args& a = p.a;
   // Persistent, balanced split: the (tile, head) items, tile-major, are cut into
   // gridDim.x equal contiguous ranges; a CTA plans a tile once for all of its

@@ -86,6 +86,14 @@ QA_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, ui
   return false;
 }
 
+// ---------------- programmatic dependent launch ----------------
+// A kernel launched with programmatic stream serialisation may start while its
+// predecessor still runs; pdl_wait() blocks until the predecessor grid has
+// completed and its memory is visible (a no-op for a normal launch).
+// pdl_launch_dependents() lets this grid's dependents start early.
+QA_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+QA_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------- TMA ----------------
 QA_DEVINL void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
                            int c3) {

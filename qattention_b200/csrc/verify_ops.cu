@@ -17,10 +17,15 @@
 namespace qa {
 namespace {
 
+// Lets a programmatically dependent successor (the next W4A16 GEMM, which waits
+// for this kernel's output before reading it) launch and stage its weights now.
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // One CTA per token row; 256 threads, 8 fp16 per 16-byte vector.
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(__half* __restrict__ h, const __half* __restrict__ delta,
                                                           const __half* __restrict__ w, __half* __restrict__ out,
                                                           int hidden, float eps) {
+  if (threadIdx.x == 0) allow_dependents();
   const int64_t row = blockIdx.x;
   __half* hr = h + row * hidden;
   const __half* dr = delta ? delta + row * hidden : nullptr;
@@ -78,6 +83,7 @@ __global__ void __launch_bounds__(256) rope_qkv_kernel(__half* __restrict__ qkv,
                                                        __half* __restrict__ vc, int M, int n_per_seq, int hq, int hkv,
                                                        int D, int64_t kv_stride_b, int64_t kv_stride_h,
                                                        int kv_offset) {
+  if (threadIdx.x == 0) allow_dependents();
   const int64_t gw = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int heads = hq + 2 * hkv;
@@ -104,6 +110,7 @@ __global__ void __launch_bounds__(256) rope_qkv_kernel(__half* __restrict__ qkv,
 
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __half* __restrict__ gu, __half* __restrict__ out,
                                                        int64_t M, int F) {
+  if (threadIdx.x == 0) allow_dependents();
   const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;  // 8 outputs per thread
   if (i >= M * F) return;
   const int64_t m = i / F, f = i % F;

@@ -40,6 +40,8 @@ constexpr int kSBytes = 128 * 2;              // 256 B of scales
 __global__ void __launch_bounds__(256) w4a16_reduce_kernel(const float* __restrict__ part, __half* __restrict__ y,
                                                           int64_t y_stride, int M, int N, int splits) {
   __shared__ float4 sums[8][32];
+  sm100::pdl_wait();  // the partial sums are the GEMM's output
+  if (threadIdx.x == 0) sm100::pdl_launch_dependents();
   const int c = threadIdx.x & 31, g = threadIdx.x >> 5;
   const int64_t q = int64_t(blockIdx.x) * 32 + c;  // float4 chunk of the M x N output
   const int64_t MN4 = int64_t(M) * N / 4;
@@ -199,6 +201,7 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (tid == 0) pdl_launch_dependents();  // the next kernel may stage while this one runs
   const uint32_t tbase = tmem_base_sh;
   // TMEM columns: accumulators [1 or 2 MMA threads][FT][tn_cols], then A buffers [NA][FT][64]
   const int nacc = p.dual ? 2 : 1;
@@ -213,7 +216,22 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
     if (lane == 0) {
       prefetch_tensormap(&x_map);
       const int S = XS;  // == WS
-      int issued = 0;
+      auto issue_w = [&](int i) {  // one 8 KB bulk copy per feature tile, then the step's scales
+        const int st = i % S, kt = kt_of(i);
+        mbar_arrive_expect_tx(&bar_w_full[st], kWBytesFT + kSBytesFT);
+#pragma unroll
+        for (int t = 0; t < FT; ++t)
+          bulk_load(sW(st) + t * kWBytes, p.qweight + (int64_t(ftile * FT + t) * k_tiles + kt) * (kWBytes / 4),
+                    kWBytes, &bar_w_full[st]);
+        bulk_load(sW(st) + kWBytesFT, p.scales + int64_t(kt) * p.N + ftile * FT * 128, kSBytesFT, &bar_w_full[st]);
+      };
+      // The weights do not depend on the previous kernel: the first stages
+      // stream while it finishes (programmatic dependent launch); only a few,
+      // so that the first activation tile does not queue behind many of them.
+      const int pre = min(nk, min(S, 3));
+      for (int i = 0; i < pre; ++i) issue_w(i);
+      pdl_wait();  // the activations are the previous kernel's output
+      int issued_x = 0, issued_w = pre;
       for (int i = 0; i < nk; ++i) {
         const int st = i % S, kt = kt_of(i);
         if (i >= S) {
@@ -223,20 +241,19 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
         }
         mbar_arrive_expect_tx(&bar_x_full[st], x_bytes);
         tma_load_3d(sX(st), &x_map, &bar_x_full[st], 0, mblk * tn, kt * 2);
-        // one 8 KB bulk copy per feature tile, then the step's scales
-        mbar_arrive_expect_tx(&bar_w_full[st], kWBytesFT + kSBytesFT);
-#pragma unroll
-        for (int t = 0; t < FT; ++t)
-          bulk_load(sW(st) + t * kWBytes, p.qweight + (int64_t(ftile * FT + t) * k_tiles + kt) * (kWBytes / 4),
-                    kWBytes, &bar_w_full[st]);
-        bulk_load(sW(st) + kWBytesFT, p.scales + int64_t(kt) * p.N + ftile * FT * 128, kSBytesFT, &bar_w_full[st]);
-        issued = i + 1;
+        issued_x = i + 1;
+        if (i >= pre) {
+          issue_w(i);
+          issued_w = i + 1;
+        }
       }
       if (abort_flag) {  // let the issued copies land before shared memory is released
-        for (int i = max(0, issued - S); i < issued; ++i) {
+        for (int i = max(0, issued_x - S); i < issued_x; ++i) {
           uint32_t n = 0;
           while (!mbar_try_wait(&bar_x_full[i % S], (i / S) & 1) && ++n < kSleepLimit) {}
-          n = 0;
+        }
+        for (int i = max(0, issued_w - S); i < issued_w; ++i) {
+          uint32_t n = 0;
           while (!mbar_try_wait(&bar_w_full[i % S], (i / S) & 1) && ++n < kSleepLimit) {}
         }
       }
@@ -505,17 +522,36 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
     attr[ai] = true;
   }
   const int threads = 96 + sh.ft * 256;
+  // both kernels are launched as programmatic dependents of their predecessor
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(unsigned(threads));
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = st;
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
   if (split) {
     p.y = a.workspace;
     p.y_stride = a.N;
-    kern<<<grid, threads, smem, st>>>(xm, p);
+    if (cudaLaunchKernelEx(&cfg, kern, xm, p) != cudaSuccess) return QA_ERR_LAUNCH;
     const int64_t vec = int64_t(a.M) * a.N / 4;
-    w4a16_reduce_kernel<<<unsigned((vec + 31) / 32), 256, 0, st>>>(
-        a.workspace, reinterpret_cast<__half*>(a.y), a.y_stride, a.M, a.N, splits);
+    cudaLaunchConfig_t rcfg = {};
+    rcfg.gridDim = dim3(unsigned((vec + 31) / 32));
+    rcfg.blockDim = dim3(256u);
+    rcfg.stream = st;
+    rcfg.attrs = pdl;
+    rcfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&rcfg, w4a16_reduce_kernel, const_cast<const float*>(a.workspace),
+                           reinterpret_cast<__half*>(a.y), int64_t(a.y_stride), int(a.M), int(a.N), splits) !=
+        cudaSuccess)
+      return QA_ERR_LAUNCH;
   } else {
     p.y = a.y;
     p.y_stride = a.y_stride;
-    kern<<<grid, threads, smem, st>>>(xm, p);
+    if (cudaLaunchKernelEx(&cfg, kern, xm, p) != cudaSuccess) return QA_ERR_LAUNCH;
   }
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
