@@ -46,7 +46,7 @@ constexpr int kBM = 128;    // packed query rows per CTA (= TMEM lanes)
 constexpr int kBN = 64;     // keys per tile
 constexpr int kStages = 4;  // K/V ring depth
 constexpr int kThreads = 224;  // warps 0-3 softmax, 4 Q/K producer, 5 MMA, 6 V producer
-constexpr uint32_t kTmemCols = 256;  // 2 x S (64) + O (<= 128)
+constexpr uint32_t kTmemCols = 512;  // 2 x S (64) + O (<= 128) + Q (<= 64)
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr float kLazy = 8.f;
 
@@ -94,7 +94,8 @@ QA_DEVINL float2 add2(float2 a, float2 b) {
 template <typename T, int D>
 __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase, int warp, int lane,
                                              int b, int hk, int n0, uint64_t* s_full,
-                                             uint64_t* p_full, uint64_t* o_done,
+                                             uint64_t* p_full, uint64_t* o_done, uint64_t* q_smem_full,
+                                             uint64_t* q_tmem_full, uint32_t sq_addr,
                                              volatile int* abort) {
   using namespace sm100;
   const uint32_t tl = tbase + (uint32_t(warp * 32) << 16);  // this warp's TMEM lanes
@@ -102,6 +103,28 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
   const int ntiles = p.n_tiles;
   float m = -INFINITY, l = 0.f;
   bool ok = true;
+  // ---- Q into TMEM (the A operand of S = Q K^T): each thread moves its own
+  // row out of the 128-byte-swizzled shared tile, so the S MMAs read only K
+  // from shared memory ----
+  {
+    ok = __all_sync(0xffffffffu, mbar_wait(q_smem_full, 0, abort, kWaitLimit));
+    if (!ok) return;
+    const int r = warp * 32 + lane;
+#pragma unroll
+    for (int hb = 0; hb < D / 64; ++hb) {  // 64-element halves of D
+      uint32_t qv[32];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = lds128(sq_addr + hb * kBM * 128 + r * 128 + ((c ^ (r & 7)) << 4));
+        qv[4 * c] = v.x; qv[4 * c + 1] = v.y; qv[4 * c + 2] = v.z; qv[4 * c + 3] = v.w;
+      }
+      tmem_st32(tl + 2 * kBN + D + hb * 32, qv);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_tmem_full);
+  }
   for (int j = 0; j < ntiles; ++j) {
     ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort, kWaitLimit));
     if (!ok) break;
@@ -214,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto sK = [&](int st) { return base + PfxSmem<D>::Q_BYTES + st * 2 * PfxSmem<D>::KV_BYTES; };
   auto sV = [&](int st) { return sK(st) + PfxSmem<D>::KV_BYTES; };
 
-  __shared__ __align__(8) uint64_t bar_q, bar_kv_full[kStages], bar_kv_empty[kStages];
+  __shared__ __align__(8) uint64_t bar_q, bar_qt, bar_kv_full[kStages], bar_kv_empty[kStages];
   __shared__ __align__(8) uint64_t bar_s_full[2], bar_p_full[2], bar_o_done, bar_final;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -230,6 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(&bar_q, 1);
+    mbar_init(&bar_qt, 4);  // Q copied into TMEM by the four softmax warps
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bar_kv_full[s], 2);  // K producer + V producer
       mbar_init(&bar_kv_empty[s], 1);
@@ -293,7 +317,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Offsets go into the 16-byte-unit address field (bits 0-13), which
       // shared-memory offsets never carry out of.
       constexpr uint32_t kStageUnits = uint32_t(2 * PfxSmem<D>::KV_BYTES) >> 4;
-      const uint64_t q_desc = sw128_desc(smem_addr(sQ), 16, 1024);
       const uint64_t k_desc0 = sw128_desc(smem_addr(sK(0)), 16, 1024);
       const uint64_t v_desc0 = sw128_desc(smem_addr(sV(0)), kBN * 128, 1024);
       auto issue_pv = [&](int i) -> bool {
@@ -308,7 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&bar_kv_empty[i % kStages]);
         return true;
       };
-      bool ok = mbar_wait(&bar_q, 0, &abort_flag, kWaitLimit);
+      bool ok = mbar_wait(&bar_qt, 0, &abort_flag, kWaitLimit);
+      const uint32_t q_tmem = tbase + 2 * kBN + D;
       for (int j = 0; ok && j < ntiles; ++j) {
         const int st = j % kStages;
         if (!mbar_wait(&bar_kv_full[st], (j / kStages) & 1, &abort_flag, kWaitLimit)) break;
@@ -317,8 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t s_tmem = tbase + (j & 1) * kBN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(s_tmem, q_desc + uint64_t((kk / 4) * kBM * 8 + (kk % 4) * 2),
-                 k_desc + uint64_t((kk / 4) * kBN * 8 + (kk % 4) * 2), idesc_s, kk > 0 ? 1u : 0u);
+          mma_ts(s_tmem, q_tmem + kk * 8, k_desc + uint64_t((kk / 4) * kBN * 8 + (kk % 4) * 2), idesc_s,
+                 kk > 0 ? 1u : 0u);
         mma_commit(&bar_s_full[j & 1]);
         if (j >= 1) ok = issue_pv(j - 1);
       }
@@ -329,8 +353,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (!mbar_try_wait(&bar_final, 0) && ++n < kWaitLimit) {}
     }
   } else {
-    softmax_role<T, D>(p, tbase, warp, lane, b, hk, n0, &bar_s_full[0], &bar_p_full[0], &bar_o_done,
-                       &abort_flag);
+    softmax_role<T, D>(p, tbase, warp, lane, b, hk, n0, &bar_s_full[0], &bar_p_full[0], &bar_o_done, &bar_q,
+                       &bar_qt, smem_addr(sQ), &abort_flag);
   }
 
   tc_fence_before();
