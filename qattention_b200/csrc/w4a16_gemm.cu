@@ -461,22 +461,31 @@ GemmShape gemm_shape(int M, int N) {
   return ft2 ? GemmShape{2, 128, 1} : GemmShape{1, 256, 1};
 }
 
-// Split-K factor for the GEMM kernel: minimise (waves of CTAs) x (K steps per
-// CTA + pipeline fill of ~4 steps), plus the reduce pass when split.
+// Split-K factor for the GEMM kernel. Unit = one K step of one CTA running
+// alone on its SM (~1 us); two CTAs sharing an SM each take ~1.4 units per
+// step (measured), so a wave costs (steps per CTA) x (1 or 1.4, by the busiest
+// SM's CTA count) + ~4 units of pipeline fill. The reduce pass reads splits x
+// M x N fp32 partials (~3 TB/s) and costs a launch (~2 units). Every split
+// count is tried (the best ones are often not powers of two).
 int w4a16_auto_splits(int M, int N, int K) {
   const GemmShape sh = gemm_shape(M, N);
   const int tiles = ((M + sh.tn - 1) / sh.tn) * (N / (128 * sh.ft));
   const int k_tiles = K / kBK;
-  const int sms = sm_count() * sh.cps;  // resident CTA slots
+  const int sms = sm_count();
   int best = 1;
   double best_cost = 1e30;
-  for (int s = 1; s <= k_tiles && s <= 64; s *= 2) {
+  for (int s = 1; s <= k_tiles && s <= 32; ++s) {
     const int per = (k_tiles + s - 1) / s;
-    const int ctas = tiles * ((k_tiles + per - 1) / per);
-    // unit = one K step (~1.2 us); the reduce reads splits x M x N fp32 partials
-    // (~3 TB/s) and costs a launch (~2 us)
-    const double reduce = s > 1 ? 2.0 + double(s) * M * N * 4 / 3.0e12 / 1.2e-6 : 0.0;
-    const double cost = double((ctas + sms - 1) / sms) * (per + 4) + reduce;
+    const int splits = (k_tiles + per - 1) / per;
+    if (splits != s) continue;  // same partition as a smaller count
+    const int64_t ctas = int64_t(tiles) * splits;
+    const int64_t slots = int64_t(sms) * sh.cps;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const int64_t in_wave = ctas < slots ? ctas : slots;
+    const int busiest = int((in_wave + sms - 1) / sms);  // CTAs on the busiest SM
+    const double step = busiest >= 2 ? 1.4 : 1.0;
+    const double reduce = s > 1 ? 2.0 + double(s) * M * N * 4 / 3.0e12 / 1.0e-6 : 0.0;
+    const double cost = double(waves) * (per * step + 4) + reduce;
     if (cost < best_cost) { best_cost = cost; best = s; }
   }
   return best;
