@@ -72,6 +72,8 @@ QA_DEVINL uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
+QA_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> QA_DEVINL void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 // 16-byte cp.async.cg to a shared-window address
 QA_DEVINL void cp_async16_s(uint32_t saddr, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gmem) : "memory");
@@ -230,7 +232,6 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
     }
   }
-  int hk_staged = -1;
   // Staging: thread tid copies 16-byte chunk my_cc of rows my_r0, my_r0 + RPP,
   // ...; the swizzle term of those rows is my_x, flipped by kXStep per pass
   // (RPP is a multiple of 8, or 4 for head_dim 256).
@@ -240,30 +241,44 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   const int my_cc = tid % RC, my_r0 = tid / RC;
   const uint32_t my_x = uint32_t((my_cc ^ (my_r0 & 7)) << 4);
   const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
-  for (int h = h_first; h < h_end; ++h) {
-  // ---- stage this head's Q rows, and K/V rows when the KV head changes ----
-  const int hk = h / p.head_ratio;
-  {
+  // Software pipeline over the heads (two cp.async groups per head): head h+1's
+  // Q and K rows load during head h's P.V and epilogue, and its V rows during
+  // its own S and softmax. K and V are re-staged only when the KV head changes;
+  // the epilogue stages the output tile in the V rows only when they are about
+  // to be replaced (otherwise it stores straight from the fragments).
+  int k_staged = -1, v_staged = -1;
+  auto issue_qk = [&](int hh) {
     const char* src = reinterpret_cast<const char*>(a.q) +
-                      int64_t(sizeof(T)) * (int64_t(h) * a.q_stride_h + (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8);
+                      int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8);
     const int64_t step = int64_t(RPP) * a.q_stride_t * int64_t(sizeof(T));
     uint32_t d = sQa + uint32_t(my_r0 * D * 2), x = my_x;
     for (int r = my_r0; r < nq; r += RPP, src += step, d += kRowStep, x ^= kXStep) cp_async16_s(d + x, src);
-  }
-  if (hk != hk_staged) {
-    const char* Kh = reinterpret_cast<const char*>(a.k) + int64_t(sizeof(T)) * (int64_t(hk) * a.k_stride_h + my_cc * 8);
-    const char* Vh = reinterpret_cast<const char*>(a.v) + int64_t(sizeof(T)) * (int64_t(hk) * a.v_stride_h + my_cc * 8);
-    uint32_t d = uint32_t(my_r0 * D * 2), x = my_x;
-    for (int j = my_r0; j < nrows; j += RPP, d += kRowStep, x ^= kXStep) {
-      const longlong2 off = *reinterpret_cast<const longlong2*>(row_off + 2 * j);
-      cp_async16_s(sKa + d + x, Kh + off.x);
-      cp_async16_s(sVa + d + x, Vh + off.y);
+    const int hk = hh / p.head_ratio;
+    if (hk != k_staged) {
+      const char* Kh = reinterpret_cast<const char*>(a.k) + int64_t(sizeof(T)) * (int64_t(hk) * a.k_stride_h + my_cc * 8);
+      uint32_t dk = uint32_t(my_r0 * D * 2), xk = my_x;
+      for (int j = my_r0; j < nrows; j += RPP, dk += kRowStep, xk ^= kXStep)
+        cp_async16_s(sKa + dk + xk, Kh + row_off[2 * j]);
+      k_staged = hk;
     }
-    hk_staged = hk;
-  }
-  cp_async_wait_all();
+    cp_async_commit();
+  };
+  auto issue_v = [&](int hh) {
+    const int hk = hh / p.head_ratio;
+    if (hk != v_staged) {
+      const char* Vh = reinterpret_cast<const char*>(a.v) + int64_t(sizeof(T)) * (int64_t(hk) * a.v_stride_h + my_cc * 8);
+      uint32_t dv = uint32_t(my_r0 * D * 2), xv = my_x;
+      for (int j = my_r0; j < nrows; j += RPP, dv += kRowStep, xv ^= kXStep)
+        cp_async16_s(sVa + dv + xv, Vh + row_off[2 * j + 1]);
+      v_staged = hk;
+    }
+    cp_async_commit();
+  };
+  issue_qk(h_first);
+  issue_v(h_first);
+  for (int h = h_first; h < h_end; ++h) {
+  cp_async_wait_group<1>();  // Q and K of head h (its V may still be in flight)
   __syncthreads();
-  if (wn > 0) {
   // ---- S = Q . K_list^T over every level's keys at once (registers) ----
   // A-operand (and stmatrix) lane address of 16x16 block kk of this warp's
   // rows: row wrow + (lane & 15), chunk 2kk + (lane >> 4), i.e.
@@ -343,6 +358,11 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   }
   const float inv0 = g < wn ? 1.f / l0 : 0.f;
   const float inv1 = g + 8 < wn ? 1.f / l1 : 0.f;
+  __syncthreads();  // every warp holds its Q fragments and is done with the K rows
+  const bool next = h + 1 < h_end;
+  if (next) issue_qk(h + 1); else cp_async_commit();
+  cp_async_wait_group<1>();  // V of head h
+  __syncthreads();
 
   // ---- O = prefix weight * prefix_o + P . V_list (P from the S registers) ----
   float o[NB][4];
@@ -403,17 +423,22 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     }
   }
 
-  // ---- epilogue: stage the tile in this warp's Q rows (stmatrix), store rows ----
+  // ---- epilogue ----
+  const bool v_replaced = !next || (h + 1) / p.head_ratio != v_staged;
+  if (v_replaced) {
+  // stage the tile in the V rows wrow.. (stmatrix), then 16-byte row stores
+  __syncthreads();  // every warp is done with the V rows
+  const uint32_t e_off = q_off - sQa + sVa;
 #pragma unroll
   for (int jj = 0; jj < D / 16; ++jj)
-    stsm_x4((q_off ^ uint32_t((jj & 3) << 5)) + uint32_t((jj >> 2) * 128), pack2<T>(o[2 * jj][0], o[2 * jj][1]),
+    stsm_x4((e_off ^ uint32_t((jj & 3) << 5)) + uint32_t((jj >> 2) * 128), pack2<T>(o[2 * jj][0], o[2 * jj][1]),
             pack2<T>(o[2 * jj][2], o[2 * jj][3]), pack2<T>(o[2 * jj + 1][0], o[2 * jj + 1][1]),
             pack2<T>(o[2 * jj + 1][2], o[2 * jj + 1][3]));
   __syncwarp();
   {
     constexpr int RPI = 32 / RC;  // rows per store instruction (power of two)
     const int c = lane % RC, r0 = lane / RC;
-    const uint32_t s0 = sQa + uint32_t((wrow + r0) * D * 2) + uint32_t((c ^ r0) << 4);
+    const uint32_t s0 = sVa + uint32_t((wrow + r0) * D * 2) + uint32_t((c ^ r0) << 4);
     const char* dst = reinterpret_cast<const char*>(a.o) +
                       int64_t(sizeof(T)) * (int64_t(h) * a.o_stride_h + (int64_t(q0) + wq_lo + r0) * a.o_stride_t + c * 8);
     const int64_t dstep = int64_t(RPI) * a.o_stride_t * int64_t(sizeof(T));
@@ -425,9 +450,19 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       dst += dstep;
     }
   }
-  }  // wn > 0
-  __syncthreads();  // shared tiles are overwritten by the next head
+  __syncthreads();  // the staged tiles are read before the next V rows land
+  } else {
+    // V rows stay for the next head of the group: store pairs from the fragments
+    T* orow = reinterpret_cast<T*>(a.o) + int64_t(h) * a.o_stride_h + (int64_t(q0) + wq_lo + g) * a.o_stride_t + 2 * t;
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      if (g < wn) *reinterpret_cast<uint32_t*>(orow + 8 * j) = pack2<T>(o[j][0], o[j][1]);
+      if (g + 8 < wn) *reinterpret_cast<uint32_t*>(orow + 8 * a.o_stride_t + 8 * j) = pack2<T>(o[j][2], o[j][3]);
+    }
+  }
+  if (next) issue_v(h + 1); else cp_async_commit();
   }  // heads
+  __syncthreads();  // shared tiles are re-planned for the next tile
   }  // tiles
 }
 
