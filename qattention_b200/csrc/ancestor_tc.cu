@@ -26,6 +26,7 @@
 // Used when every walk level of a tile fits in shared memory (always true for
 // b >= 2; chains up to depth ~300), for head_dim 64, 128 and 256.
 #include <atomic>
+#include <mutex>
 
 #include "ancestor_plan.cuh"
 
@@ -41,7 +42,7 @@ constexpr int kTcMaxKeys = 128;  // key-list columns per warp (all walk levels o
 struct TcParams {
   qa_ancestor_args a;
   float scale_log2;
-  int32_t tiles_per_seq;
+  TileGeom geom;  // tiling of every sequence's tree
   int32_t head_ratio;
   int32_t rows_cap;
   int32_t kw_cap;  // key-list columns per warp (multiple of 16)
@@ -122,7 +123,7 @@ template <int D> struct TcSmem {
 
 // MINB = CTAs per SM the register allocation must allow (1, 3 or 4; chosen
 // per launch by launch_tc_minb).
-template <typename T, int D, int NBK, int MINB>
+template <typename T, int D, int NBK, int MINB, bool SUB>
 __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcParams p) {
   using SM = TcSmem<D>;
   constexpr int RC = D / 8;   // 16-byte chunks per row
@@ -135,14 +136,17 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   unsigned char* sK = smem_base + SM::k_off();
   unsigned char* sV = smem_base + SM::v_off(p.rows_cap);
   int64_t* row_off = reinterpret_cast<int64_t*>(smem_base + SM::tok_off(p.rows_cap));
-  __shared__ int lv_off[kMaxLevels];
-  __shared__ int win_lo[kMaxLevels + 1];
-  __shared__ int win_base[kMaxLevels + 1];
-  __shared__ int n_staged, n_win;
-  __shared__ int w_col[kWarps][kMaxLevels];       // column = w_col[s] + node, per warp
-  __shared__ int w_lo[kWarps][kMaxLevels + 1];    // per-warp key windows
-  __shared__ int w_base[kWarps][kMaxLevels + 1];
-  __shared__ int w_levels[kWarps], w_nwin[kWarps];
+  __shared__ int seg_lo[kMaxLevels + 1], seg_row[kMaxLevels + 2], n_seg;  // the tile's level segments
+  __shared__ int q_node[kTcMQ];                   // tree node of every tile row
+  __shared__ int win_lo[kMaxWin + 1];             // staged windows (descending nodes)
+  __shared__ int win_base[kMaxWin + 1];
+  __shared__ int n_win;
+  __shared__ int w_lo[kWarps][kMaxWin + 1];       // per-warp key windows
+  __shared__ int w_base[kWarps][kMaxWin + 1];
+  __shared__ int w_nwin[kWarps];
+  __shared__ int lv_off[kMaxLevels];              // contiguous tiles: CTA level offsets (unused after planning)
+  __shared__ int w_col[kWarps][kMaxLevels];       // contiguous tiles: column = w_col[s] + node, per warp
+  __shared__ int w_levels[kWarps];
   __shared__ int kslot[kWarps][kTcMaxKeys];       // staged K/V row of each key column
 
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a following GEMM may stage
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   // Persistent, balanced split: the (tile, head) items, tile-major, are cut into
   // gridDim.x equal contiguous ranges; a CTA plans a tile once for all of its
   // heads in the range (at most a few tiles per CTA).
-  const int64_t items = int64_t(a.batch) * p.tiles_per_seq * a.num_q_heads;
+  const int64_t items = int64_t(a.batch) * p.geom.tiles * a.num_q_heads;
   int64_t it = items * blockIdx.x / gridDim.x;
   const int64_t it_end = items * (blockIdx.x + 1) / gridDim.x;
   while (it < it_end) {
@@ -158,28 +162,64 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   const int h_first = int(it - tg * a.num_q_heads);
   const int h_end = int(min(int64_t(a.num_q_heads), h_first + (it_end - it)));
   it += h_end - h_first;
-  const int tile = int(tg % p.tiles_per_seq);
-  const int seq = int(tg / p.tiles_per_seq);
+  const int tile = int(tg % p.geom.tiles);
+  const int seq = int(tg / p.geom.tiles);
   const int q0 = __ldg(a.cu_seqlens_q + seq);
   const int len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
-  const int q_lo = tile * kTcMQ;
-  if (q_lo >= len) continue;  // uniform over the CTA
-  const int nq = min(kTcMQ, len - q_lo);
   const int kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int wrow = warp * 16;  // first tile row of this warp
-  const int wn = max(0, min(16, nq - wrow));
-  const int wq_lo = q_lo + wrow;
-
-  // ---- CTA plan (levels -> staged windows), shared by every head ----
-  if (tid == 0) {
-    int ns = 0, nw = 0;
-    plan_levels_fit(q_lo, nq, a.max_depth, p.div_b, lv_off, win_lo, win_base, ns, nw);
-    n_staged = ns;
-    n_win = nw;
+  int q_lo = 0, nq = 0, wn = 0;
+  __syncthreads();  // the previous tile's plan is no longer read
+  if constexpr (SUB) {
+    // ---- plans, shared by every head: the tile's staged windows (thread 1)
+    // and each warp's key windows (lane 0 of each warp), computed in parallel ----
+    if (tid == 0) n_seg = tile_segments(p.geom, tile, len, seg_lo, seg_row);
+    __syncthreads();
+    nq = seg_row[n_seg];
+    if (nq == 0) continue;  // uniform over the CTA
+    wn = max(0, min(16, nq - wrow));
+    if (tid < nq) {
+      int i = 0;
+      while (seg_row[i + 1] <= tid) ++i;
+      q_node[tid] = seg_lo[i] + tid - seg_row[i];
+    }
+    if ((lane == 0 && wn > 0) || tid == 1) {
+      const bool cta = tid == 1;
+      int nwin = 0;
+      plan_rows(p.geom, seg_lo, seg_row, n_seg, cta ? 0 : wrow, cta ? nq : wrow + wn, a.max_depth,
+                DevDivB{p.div_b}, cta ? win_lo : w_lo[warp], cta ? win_base : w_base[warp], nwin);
+      if (cta) n_win = nwin;
+      else w_nwin[warp] = nwin;
+    }
+    __syncthreads();
+  } else {
+    // ---- contiguous tile: its walk levels are contiguous node ranges
+    // (plan_levels_fit), for the CTA and for each warp's 16 rows ----
+    q_lo = tile * kTcMQ;
+    if (q_lo >= len) continue;  // uniform over the CTA
+    nq = min(kTcMQ, len - q_lo);
+    wn = max(0, min(16, nq - wrow));
+    if (tid == 0) {
+      int ns = 0, nw = 0;
+      plan_levels_fit(q_lo, nq, a.max_depth, p.div_b, lv_off, win_lo, win_base, ns, nw);
+      n_win = nw;
+    }
+    if (lane == 0 && wn > 0 && warp > 0) {
+      int L = 0, nwin = 0;
+      plan_levels_fit(q_lo + wrow, wn, a.max_depth, p.div_b, w_col[warp], w_lo[warp], w_base[warp], L, nwin);
+      w_levels[warp] = L;
+      w_nwin[warp] = nwin;
+    }
+    if (tid == 32) {  // warp 0's plan, beside thread 0's
+      int L = 0, nwin = 0;
+      plan_levels_fit(q_lo, min(16, nq), a.max_depth, p.div_b, w_col[0], w_lo[0], w_base[0], L, nwin);
+      w_levels[0] = L;
+      w_nwin[0] = nwin;
+    }
+    __syncthreads();
   }
-  __syncthreads();
   const int nw = n_win, nrows = win_base[nw];
   for (int j = tid; j < nrows; j += kTcThreads) {  // element offset of every staged row
     int w = 0;
@@ -188,14 +228,11 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     row_off[2 * j] = tk * a.k_stride_t * int64_t(sizeof(T));  // byte offsets
     row_off[2 * j + 1] = tk * a.v_stride_t * int64_t(sizeof(T));
   }
-  // ---- per-warp key list: the warp's level ranges merged into windows ----
-  if (lane == 0 && wn > 0) {
-    int L = 0, nwin = 0;
-    plan_levels_fit(wq_lo, wn, a.max_depth, p.div_b, w_col[warp], w_lo[warp], w_base[warp], L, nwin);
-    w_levels[warp] = L;
-    w_nwin[warp] = nwin;
-  }
-  __syncthreads();
+  // token (relative to the sequence) of tile row r
+  auto row_tok = [&](int r) -> int {
+    if constexpr (SUB) return q_node[r];
+    else return q_lo + r;
+  };
   // key column -> staged slot (columns past the list repeat its last row)
   const int nkeys = wn > 0 ? w_base[warp][w_nwin[warp]] : 0;
   const int kpad = (nkeys + 15) & ~15;
@@ -213,24 +250,56 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   }
   const int g = lane >> 2, t = lane & 3;
   const int* ks = kslot[warp];
+  // token of this thread's row g (half 0) or g + 8 (half 1), clamped to the
+  // warp's rows (the result is unused past them)
+  auto tok_g = [&](int half) -> int { return row_tok(wrow + min(g + 8 * half, max(wn - 1, 0))); };
   // ---- which fragment elements are this thread's rows' walk keys ----
-  // Row r's step-s key is column w_col[s] + node_s(r); the thread owning
-  // column c of a row holds it in block c/8, element c%2 when (c%8)/2 == t.
+  // The thread owning column c of a row holds it in block c/8, element c%2
+  // when (c%8)/2 == t.
   uint32_t sel0 = 0u, sel1 = 0u;  // same for every head
-  if (wn > 0) {
-    const int L = w_levels[warp];
-    const int* wc = w_col[warp];
-    int n0 = g < wn ? wq_lo + g : -1, n1 = g + 8 < wn ? wq_lo + g + 8 : -1;
-    for (int s = 0; s < L; ++s) {
-      if (s > 0) {
-        n0 = n0 <= 0 ? -1 : int(fast_div(uint32_t(n0 - 1), p.div_b));
-        n1 = n1 <= 0 ? -1 : int(fast_div(uint32_t(n1 - 1), p.div_b));
+  if constexpr (SUB) {
+    // row r's step-s key is the column of node_s(r) in the warp's windows (the
+    // walk descends, so the window index only grows)
+    if (wn > 0) {
+      const int* wl = w_lo[warp];
+      const int* wb = w_base[warp];
+      const int nwin = w_nwin[warp];
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        if (g + 8 * half >= wn) continue;
+        int n = tok_g(half), wi = 0;
+        uint32_t sel = 0u;
+        for (int s = 0; s <= a.max_depth; ++s) {
+          if (s > 0) {
+            if (n == 0) break;  // the walk ended at the root
+            n = int(fast_div(uint32_t(n - 1), p.div_b));
+          }
+          while (wi + 1 < nwin && n < wl[wi]) ++wi;
+          const int c = wb[wi] + n - wl[wi];
+          if (((c >> 1) & 3) == t) sel |= 1u << (((c >> 3) << 1) | (c & 1));
+        }
+        if (half) sel1 = sel; else sel0 = sel;
       }
-      const int off = wc[s];
-      const int c0 = off + n0, c1 = off + n1;
-      if (n0 >= 0 && ((c0 >> 1) & 3) == t) sel0 |= 1u << (((c0 >> 3) << 1) | (c0 & 1));
-      if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
     }
+    __syncthreads();  // row offsets are visible to every staging thread
+  } else {
+    // row r's step-s key is column w_col[s] + node_s(r)
+    if (wn > 0) {
+      const int L = w_levels[warp];
+      const int* wc = w_col[warp];
+      int n0 = g < wn ? tok_g(0) : -1, n1 = g + 8 < wn ? tok_g(1) : -1;
+      for (int s = 0; s < L; ++s) {
+        if (s > 0) {
+          n0 = n0 <= 0 ? -1 : int(fast_div(uint32_t(n0 - 1), p.div_b));
+          n1 = n1 <= 0 ? -1 : int(fast_div(uint32_t(n1 - 1), p.div_b));
+        }
+        const int off = wc[s];
+        const int c0 = off + n0, c1 = off + n1;
+        if (n0 >= 0 && ((c0 >> 1) & 3) == t) sel0 |= 1u << (((c0 >> 3) << 1) | (c0 & 1));
+        if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
+      }
+    }
+    __syncthreads();  // row offsets are visible to every staging thread
   }
   // Staging: thread tid copies 16-byte chunk my_cc of rows my_r0, my_r0 + RPP,
   // ...; the swizzle term of those rows is my_x, flipped by kXStep per pass
@@ -248,11 +317,23 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   // to be replaced (otherwise it stores straight from the fragments).
   int k_staged = -1, v_staged = -1;
   auto issue_qk = [&](int hh) {
-    const char* src = reinterpret_cast<const char*>(a.q) +
-                      int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8);
-    const int64_t step = int64_t(RPP) * a.q_stride_t * int64_t(sizeof(T));
-    uint32_t d = sQa + uint32_t(my_r0 * D * 2), x = my_x;
-    for (int r = my_r0; r < nq; r += RPP, src += step, d += kRowStep, x ^= kXStep) cp_async16_s(d + x, src);
+    if constexpr (SUB) {
+      const char* Qh = reinterpret_cast<const char*>(a.q) +
+                       int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + int64_t(q0) * a.q_stride_t + my_cc * 8);
+      const int64_t tstep = a.q_stride_t * int64_t(sizeof(T));
+      uint32_t d = sQa + uint32_t(my_r0 * D * 2), x = my_x;
+#pragma unroll
+      for (int i = 0; i < kTcMQ / RPP; ++i, d += kRowStep, x ^= kXStep) {
+        const int r = my_r0 + i * RPP;
+        if (r < nq) cp_async16_s(d + x, Qh + row_tok(r) * tstep);
+      }
+    } else {
+      const char* src = reinterpret_cast<const char*>(a.q) +
+                        int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8);
+      const int64_t step = int64_t(RPP) * a.q_stride_t * int64_t(sizeof(T));
+      uint32_t d = sQa + uint32_t(my_r0 * D * 2), x = my_x;
+      for (int r = my_r0; r < nq; r += RPP, src += step, d += kRowStep, x ^= kXStep) cp_async16_s(d + x, src);
+    }
     const int hk = hh / p.head_ratio;
     if (hk != k_staged) {
       const char* Kh = reinterpret_cast<const char*>(a.k) + int64_t(sizeof(T)) * (int64_t(hk) * a.k_stride_h + my_cc * 8);
@@ -314,9 +395,9 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   // ---- exact softmax per row over its walk (a quad of threads shares a row) ----
   float mx0 = -INFINITY, mx1 = -INFINITY, pl0 = -INFINITY, pl1 = -INFINITY;
   if (a.prefix_o != nullptr) {
-    const int64_t t0 = int64_t(q0) + wq_lo + g;
+    const int64_t t0 = int64_t(q0) + tok_g(0);
     if (g < wn) pl0 = __ldg(a.prefix_lse + t0 * a.prefix_lse_stride_t + int64_t(h) * a.prefix_lse_stride_h) * kLog2e;
-    if (g + 8 < wn) pl1 = __ldg(a.prefix_lse + (t0 + 8) * a.prefix_lse_stride_t + int64_t(h) * a.prefix_lse_stride_h) * kLog2e;
+    if (g + 8 < wn) pl1 = __ldg(a.prefix_lse + (int64_t(q0) + tok_g(1)) * a.prefix_lse_stride_t + int64_t(h) * a.prefix_lse_stride_h) * kLog2e;
     mx0 = pl0;
     mx1 = pl1;
   }
@@ -353,8 +434,8 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   l1 += wp1;
   if (a.lse != nullptr && t == 0) {
     float* Lh = a.lse + int64_t(h) * a.lse_stride_h;
-    if (g < wn) Lh[(int64_t(q0) + wq_lo + g) * a.lse_stride_t] = (mx0 + __log2f(l0)) * kLn2;
-    if (g + 8 < wn) Lh[(int64_t(q0) + wq_lo + g + 8) * a.lse_stride_t] = (mx1 + __log2f(l1)) * kLn2;
+    if (g < wn) Lh[(int64_t(q0) + tok_g(0)) * a.lse_stride_t] = (mx0 + __log2f(l0)) * kLn2;
+    if (g + 8 < wn) Lh[(int64_t(q0) + tok_g(1)) * a.lse_stride_t] = (mx1 + __log2f(l1)) * kLn2;
   }
   const float inv0 = g < wn ? 1.f / l0 : 0.f;
   const float inv1 = g + 8 < wn ? 1.f / l1 : 0.f;
@@ -375,7 +456,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       const float wgt = half ? wp1 : wp0;
       if (r >= wn || wgt == 0.f) continue;
       const float wgt_n = wgt * (half ? inv1 : inv0);
-      const int64_t tq = int64_t(q0) + wq_lo + r;
+      const int64_t tq = int64_t(q0) + tok_g(half);
       const T* po = reinterpret_cast<const T*>(a.prefix_o) + tq * a.prefix_o_stride_t + int64_t(h) * a.prefix_o_stride_h;
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
@@ -439,36 +520,49 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     constexpr int RPI = 32 / RC;  // rows per store instruction (power of two)
     const int c = lane % RC, r0 = lane / RC;
     const uint32_t s0 = sVa + uint32_t((wrow + r0) * D * 2) + uint32_t((c ^ r0) << 4);
-    const char* dst = reinterpret_cast<const char*>(a.o) +
-                      int64_t(sizeof(T)) * (int64_t(h) * a.o_stride_h + (int64_t(q0) + wq_lo + r0) * a.o_stride_t + c * 8);
-    const int64_t dstep = int64_t(RPI) * a.o_stride_t * int64_t(sizeof(T));
+    if constexpr (SUB) {
+      const char* Oh = reinterpret_cast<const char*>(a.o) +
+                       int64_t(sizeof(T)) * (int64_t(h) * a.o_stride_h + int64_t(q0) * a.o_stride_t + c * 8);
+      const int64_t tstep = a.o_stride_t * int64_t(sizeof(T));
 #pragma unroll
-    for (int it = 0; it < 16 / RPI; ++it) {
-      // row r0 + it*RPI: (r & 7) = r0 ^ ((it*RPI) & 7) since r0 < RPI
-      if (r0 + it * RPI < wn)
-        st_stream(const_cast<char*>(dst), lds128((s0 ^ uint32_t(((it * RPI) & 7) << 4)) + uint32_t(it * RPI * D * 2)));
-      dst += dstep;
+      for (int it = 0; it < 16 / RPI; ++it) {
+        // row r0 + it*RPI: (r & 7) = r0 ^ ((it*RPI) & 7) since r0 < RPI
+        if (r0 + it * RPI < wn)
+          st_stream(const_cast<char*>(Oh + row_tok(wrow + r0 + it * RPI) * tstep),
+                    lds128((s0 ^ uint32_t(((it * RPI) & 7) << 4)) + uint32_t(it * RPI * D * 2)));
+      }
+    } else {
+      const char* dst = reinterpret_cast<const char*>(a.o) +
+                        int64_t(sizeof(T)) * (int64_t(h) * a.o_stride_h + (int64_t(q0) + q_lo + wrow + r0) * a.o_stride_t + c * 8);
+      const int64_t dstep = int64_t(RPI) * a.o_stride_t * int64_t(sizeof(T));
+#pragma unroll
+      for (int it = 0; it < 16 / RPI; ++it) {
+        if (r0 + it * RPI < wn)
+          st_stream(const_cast<char*>(dst), lds128((s0 ^ uint32_t(((it * RPI) & 7) << 4)) + uint32_t(it * RPI * D * 2)));
+        dst += dstep;
+      }
     }
   }
   __syncthreads();  // the staged tiles are read before the next V rows land
   } else {
     // V rows stay for the next head of the group: store pairs from the fragments
-    T* orow = reinterpret_cast<T*>(a.o) + int64_t(h) * a.o_stride_h + (int64_t(q0) + wq_lo + g) * a.o_stride_t + 2 * t;
+    T* Oh = reinterpret_cast<T*>(a.o) + int64_t(h) * a.o_stride_h + int64_t(q0) * a.o_stride_t + 2 * t;
+    T* orow0 = Oh + tok_g(0) * a.o_stride_t;
+    T* orow1 = Oh + tok_g(1) * a.o_stride_t;
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
-      if (g < wn) *reinterpret_cast<uint32_t*>(orow + 8 * j) = pack2<T>(o[j][0], o[j][1]);
-      if (g + 8 < wn) *reinterpret_cast<uint32_t*>(orow + 8 * a.o_stride_t + 8 * j) = pack2<T>(o[j][2], o[j][3]);
+      if (g < wn) *reinterpret_cast<uint32_t*>(orow0 + 8 * j) = pack2<T>(o[j][0], o[j][1]);
+      if (g + 8 < wn) *reinterpret_cast<uint32_t*>(orow1 + 8 * j) = pack2<T>(o[j][2], o[j][3]);
     }
   }
   if (next) issue_v(h + 1); else cp_async_commit();
   }  // heads
-  __syncthreads();  // shared tiles are re-planned for the next tile
   }  // tiles
 }
 
 // Resident CTAs per SM of one instantiation at this shared-memory size
 // (memoised: the size depends only on the tree shape).
-template <typename T, int D, int NBK, int MINB>
+template <typename T, int D, int NBK, int MINB, bool SUB>
 int resident_ctas(int smem) {
   // (smem << 32 | occupancy) of the last query; atomic so that host threads
   // launching concurrently read a consistent pair
@@ -476,11 +570,11 @@ int resident_ctas(int smem) {
   const int64_t m = memo.load(std::memory_order_relaxed);
   if (m >= 0 && int(m >> 32) == smem) return int(m & 0xffffffff);
   {
-    if (cudaFuncSetAttribute(ancestor_tc_kernel<T, D, NBK, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(ancestor_tc_kernel<T, D, NBK, MINB, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kTcMaxSmem) != cudaSuccess)
       return 0;
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ancestor_tc_kernel<T, D, NBK, MINB>, kTcThreads,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ancestor_tc_kernel<T, D, NBK, MINB, SUB>, kTcThreads,
                                                       smem) != cudaSuccess)
       return 0;
     memo.store((int64_t(smem) << 32) | int64_t(occ), std::memory_order_relaxed);
@@ -488,43 +582,48 @@ int resident_ctas(int smem) {
   }
 }
 
-template <typename T, int D, int NBK, int MINB>
+template <typename T, int D, int NBK, int MINB, bool SUB>
 int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st) {
-  ancestor_tc_kernel<T, D, NBK, MINB><<<dim3{unsigned(blocks)}, kTcThreads, smem, st>>>(p);
+  ancestor_tc_kernel<T, D, NBK, MINB, SUB><<<dim3{unsigned(blocks)}, kTcThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
 
 // Picks the register budget and the persistent grid (one CTA per resident
 // slot). The kernel is latency-bound, so resident warps count: the builds
-// capped for 3 and 4 CTAs per SM (168 and 128 registers, some spills) are used
-// only when they raise residency; at equal residency the build with more
-// registers (fewer spills) runs faster. head_dim 256 is held to <= 2 CTAs by
-// shared memory and uses the unconstrained build only.
-template <typename T, int D, int NBK>
+// capped for 3 and 4 CTAs per SM (168 and 128 registers) are used only when
+// they raise residency; at equal residency the build with more registers runs
+// faster. head_dim 256 is held to <= 2 CTAs by shared memory and uses the
+// unconstrained build only.
+template <typename T, int D, int NBK, bool SUB>
 int launch_tc_minb(TcParams& p, cudaStream_t st) {
-  const int64_t items = int64_t(p.a.batch) * p.tiles_per_seq * p.a.num_q_heads;
+  const int64_t items = int64_t(p.a.batch) * p.geom.tiles * p.a.num_q_heads;
   const int smem = TcSmem<D>::total(p.rows_cap);
-  const int occ1 = resident_ctas<T, D, NBK, 1>(smem);
+  const int occ1 = resident_ctas<T, D, NBK, 1, SUB>(smem);
   int occ = occ1, minb = 1;
   if constexpr (D <= 128) {
-    const int occ3 = resident_ctas<T, D, NBK, 3>(smem);
-    const int occ4 = resident_ctas<T, D, NBK, 4>(smem);
+    const int occ3 = resident_ctas<T, D, NBK, 3, SUB>(smem);
+    const int occ4 = resident_ctas<T, D, NBK, 4, SUB>(smem);
     if (occ3 > occ) occ = occ3, minb = 3;
     if (occ4 > occ) occ = occ4, minb = 4;
   }
   if (occ <= 0) return QA_ERR_LAUNCH;
   const int64_t blocks = min(items, int64_t(p.num_sms) * occ);
   if (blocks <= 0) return QA_OK;
-  if (minb == 4) return launch_tc<T, D, NBK, 4>(p, blocks, smem, st);
-  if (minb == 3) return launch_tc<T, D, NBK, 3>(p, blocks, smem, st);
-  return launch_tc<T, D, NBK, 1>(p, blocks, smem, st);
+  if (minb == 4) return launch_tc<T, D, NBK, 4, SUB>(p, blocks, smem, st);
+  if (minb == 3) return launch_tc<T, D, NBK, 3, SUB>(p, blocks, smem, st);
+  return launch_tc<T, D, NBK, 1, SUB>(p, blocks, smem, st);
+}
+
+template <typename T, int D, int NBK>
+int launch_tc_sub(TcParams& p, cudaStream_t st) {
+  return p.geom.bands > 0 ? launch_tc_minb<T, D, NBK, true>(p, st) : launch_tc_minb<T, D, NBK, false>(p, st);
 }
 
 template <typename T, int D>
 int launch_tc_nbk(TcParams& p, cudaStream_t st) {
-  if (p.kw_cap <= 32) return launch_tc_minb<T, D, 4>(p, st);
-  if (p.kw_cap <= 64) return launch_tc_minb<T, D, 8>(p, st);
-  return launch_tc_minb<T, D, 16>(p, st);
+  if (p.kw_cap <= 32) return launch_tc_sub<T, D, 4>(p, st);
+  if (p.kw_cap <= 64) return launch_tc_sub<T, D, 8>(p, st);
+  return launch_tc_sub<T, D, 16>(p, st);
 }
 
 }  // namespace
@@ -533,23 +632,70 @@ int launch_tc_nbk(TcParams& p, cudaStream_t st) {
 // head_dim 64/128/256, every level of a tile fits in shared memory); returns
 // kTcNotApplicable otherwise so the caller runs the scalar walk. Arguments are
 // already validated by qa_ancestor_attn.
+// Tiling of a launch's trees (memoised per tree shape): contiguous tiles, or
+// subtree tiles when they stage far fewer rows per tile (deep trees; their
+// capacities come from planning every tile of a max_seqlen-node tree here).
+struct TcPlan {
+  TileGeom geom;
+  int rows_cap = 0, kw_cap = 0;
+};
+bool tc_plan(int b, int max_depth, int n, TcPlan& out) {
+  static std::mutex mu;
+  static int key_b = -1, key_d = -1, key_n = -1;
+  static TcPlan memo;
+  static bool memo_ok = false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (b != key_b || max_depth != key_d || n != key_n) {
+    memo_ok = false;
+    // contiguous tiles: the level-range bounds plan_levels_fit stays within
+    const int rows_c = rows_needed(kTcMQ, b, max_depth, false);
+    const int kw_c = (rows_needed(16, b, max_depth, false) + 15) & ~15;
+    if (kw_c <= kTcMaxKeys) {
+      memo.geom = make_tile_geom(b, n, false);
+      memo.rows_cap = max(rows_c, kTcMQ);  // the epilogue stages the output tile in the V rows
+      memo.kw_cap = kw_c;
+      memo_ok = true;
+    }
+    // subtree tiles, when they stage under two thirds of the rows (deep
+    // trees); shallower trees keep the cheaper contiguous planning
+    const TileGeom gs = make_tile_geom(b, n, true);
+    if (gs.bands > 0) {
+      int rows = 0, keys = 0;
+      tile_geom_caps(gs, n, max_depth, rows, keys);
+      rows = max(rows, kTcMQ);
+      const int kw = max((keys + 15) & ~15, 16);
+      if (kw <= kTcMaxKeys && (!memo_ok || 3 * rows < 2 * memo.rows_cap)) {
+        memo.geom = gs;
+        memo.rows_cap = rows;
+        memo.kw_cap = kw;
+        memo_ok = true;
+      }
+    }
+    key_b = b;
+    key_d = max_depth;
+    key_n = n;
+  }
+  out = memo;
+  return memo_ok;
+}
+
 int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
   if (a.parents != nullptr) return kTcNotApplicable;
   if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return kTcNotApplicable;
-  if (a.branching == 1 && a.max_depth >= kMaxLevels) return kTcNotApplicable;
-  const int rows = rows_needed(kTcMQ, a.branching, a.max_depth, false);
-  const int kw = (rows_needed(16, a.branching, a.max_depth, false) + 15) & ~15;
-  if (kw > kTcMaxKeys) return kTcNotApplicable;
+  if (a.branching < 2 || a.max_seqlen <= 0) return kTcNotApplicable;  // chains: the scalar walk
+  TcPlan plan;
+  if (!tc_plan(a.branching, a.max_depth, a.max_seqlen, plan)) return kTcNotApplicable;
+  const int rows = plan.rows_cap;
   const int smem = a.head_dim == 64 ? TcSmem<64>::total(rows)
                  : a.head_dim == 128 ? TcSmem<128>::total(rows) : TcSmem<256>::total(rows);
   if (smem > kTcMaxSmem) return kTcNotApplicable;
   TcParams p;
   p.a = a;
   p.scale_log2 = a.scale * kLog2e;
-  p.tiles_per_seq = (a.max_seqlen + kTcMQ - 1) / kTcMQ;
+  p.geom = plan.geom;
   p.head_ratio = a.num_q_heads / a.num_kv_heads;
   p.rows_cap = rows;
-  p.kw_cap = kw;
+  p.kw_cap = plan.kw_cap;
   {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
