@@ -46,7 +46,8 @@ struct TcParams {
   int32_t head_ratio;
   int32_t rows_cap;
   int32_t kw_cap;  // key-list columns per warp (multiple of 16)
-  int32_t num_sms;  // host-side launch planning only
+  int32_t num_sms;     // host-side launch planning only
+  int32_t unit_heads;  // > 0: CTA x runs unit x = (tile, chunk of unit_heads heads)
   FastDiv div_b;
 };
 
@@ -151,12 +152,21 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
 
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a following GEMM may stage
   const qa_ancestor_args& a = p.a;
-  // Persistent, balanced split: the (tile, head) items, tile-major, are cut into
-  // gridDim.x equal contiguous ranges; a CTA plans a tile once for all of its
-  // heads in the range (at most a few tiles per CTA).
+  // Work of this CTA: either an equal contiguous range of the (tile, head)
+  // items, tile-major (a persistent grid; the range touches one or two
+  // tiles), or one unit = one tile and a chunk of its heads. A tile is
+  // planned once for all of its heads in the range.
   const int64_t items = int64_t(a.batch) * p.geom.tiles * a.num_q_heads;
-  int64_t it = items * blockIdx.x / gridDim.x;
-  const int64_t it_end = items * (blockIdx.x + 1) / gridDim.x;
+  int64_t it, it_end;
+  if (p.unit_heads > 0) {  // one tile, one chunk of heads: every CTA plans exactly one tile
+    const int chunks = (a.num_q_heads + p.unit_heads - 1) / p.unit_heads;
+    const int64_t tg = blockIdx.x / chunks;
+    it = tg * a.num_q_heads + int64_t(blockIdx.x % chunks) * p.unit_heads;
+    it_end = min(it + p.unit_heads, (tg + 1) * a.num_q_heads);
+  } else {
+    it = items * blockIdx.x / gridDim.x;
+    it_end = items * (blockIdx.x + 1) / gridDim.x;
+  }
   while (it < it_end) {
   const int64_t tg = it / a.num_q_heads;
   const int h_first = int(it - tg * a.num_q_heads);
@@ -607,7 +617,29 @@ int launch_tc_minb(TcParams& p, cudaStream_t st) {
     if (occ4 > occ) occ = occ4, minb = 4;
   }
   if (occ <= 0) return QA_ERR_LAUNCH;
-  const int64_t blocks = min(items, int64_t(p.num_sms) * occ);
+  int64_t blocks = min(items, int64_t(p.num_sms) * occ);
+  // Work split. A tile's plan costs about as much as kPlanHeads heads (the
+  // subtree planner more), so an even split of the (tile, head) items, whose
+  // ranges touch one or two tiles, is compared with one (tile, head-chunk)
+  // unit per CTA when every unit gets a slot; the cheaper estimate wins.
+  p.unit_heads = 0;
+  {
+    const double plan = SUB ? 2.0 : 1.2;  // tile plan cost in heads (measured)
+    const int H = p.a.num_q_heads;
+    const int64_t tgs = int64_t(p.a.batch) * p.geom.tiles;
+    const double even = double((items + blocks - 1) / blocks) + 2.0 * plan;
+    double best = even;
+    for (int q = H; q >= 1; --q) {
+      const int chunks = (H + q - 1) / q;
+      if (tgs * chunks > int64_t(p.num_sms) * occ) break;
+      if ((H + chunks - 1) / chunks != q) continue;  // same chunks as a smaller q
+      if (plan + q < best) {
+        best = plan + q;
+        p.unit_heads = q;
+      }
+    }
+    if (p.unit_heads > 0) blocks = tgs * ((H + p.unit_heads - 1) / p.unit_heads);
+  }
   if (blocks <= 0) return QA_OK;
   if (minb == 4) return launch_tc<T, D, NBK, 4, SUB>(p, blocks, smem, st);
   if (minb == 3) return launch_tc<T, D, NBK, 3, SUB>(p, blocks, smem, st);
