@@ -14,13 +14,13 @@
 //     G = Hq/Hkv query heads sharing a KV head are packed as rows (token, g),
 //     so K/V tiles are read once for all of them (no repeat_kv copies).
 //   * TMA (5-D tensor maps over [B, tokens, heads, D] with D split into its
-//     two 64-element halves, 128-byte swizzle) streams 64-key K and V tiles
-//     through a 4-stage shared-memory ring, one copy per tile (both halves)
+//     two 64-element halves, 128-byte swizzle) streams 128-key K and V tiles
+//     through a 3-stage shared-memory ring, one copy per tile (both halves)
 //     and K and V issued by two different threads: a single issuing thread
 //     sustains only a few TMA copies per microsecond. The Q tile is loaded
 //     once. Every copy lands in this CTA's own shared memory only.
 //   * One thread issues tcgen05.mma: S_j = Q K_j^T into one of two TMEM
-//     buffers (fp32, 64 columns), then O += P_{j-1} V_{j-1} with P read from
+//     buffers (fp32, 128 columns), then O += P_{j-1} V_{j-1} with P read from
 //     TMEM (the fp16/bf16 probabilities overwrite their S buffer) and V from
 //     shared memory; commits drive the mbarriers.
 //   * Four softmax warps own one accumulator row each (TMEM lane = row): read
@@ -43,10 +43,10 @@ __device__ int g_prefix_error = 0;
 namespace {
 
 constexpr int kBM = 128;    // packed query rows per CTA (= TMEM lanes)
-constexpr int kBN = 64;     // keys per tile
-constexpr int kStages = 4;  // K/V ring depth
+constexpr int kBN = 128;    // keys per tile (S MMAs with N = 128 run at the full tensor rate)
+constexpr int kStages = 3;  // K/V ring depth
 constexpr int kThreads = 224;  // warps 0-3 softmax, 4 Q/K producer, 5 MMA, 6 V producer
-constexpr uint32_t kTmemCols = 512;  // 2 x S (64) + O (<= 128) + Q (<= 64)
+constexpr uint32_t kTmemCols = 512;  // 2 x S (128) + O (<= 128) + Q (<= 64)
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr float kLazy = 8.f;
 
@@ -129,26 +129,30 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
     ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort, kWaitLimit));
     if (!ok) break;
     tc_fence_after();
-    uint32_t r0[32], r1[32];
-    tmem_ld32(tl + (j & 1) * kBN, r0);
-    tmem_ld32(tl + (j & 1) * kBN + 32, r1);
+    constexpr int NC = kBN / 32;  // 32-column chunks of the S tile
+    uint32_t r[NC][32];
+#pragma unroll
+    for (int ch = 0; ch < NC; ++ch) tmem_ld32(tl + (j & 1) * kBN + 32 * ch, r[ch]);
     tmem_wait_ld();
     const int kvalid = min(kBN, p.prefix_len - j * kBN);  // keys past L were zero-filled
     if (kvalid < kBN) {  // only the last tile is partial
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        if (c >= kvalid) r0[c] = __float_as_uint(-INFINITY);
-        if (c + 32 >= kvalid) r1[c] = __float_as_uint(-INFINITY);
-      }
+      for (int ch = 0; ch < NC; ++ch)
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (32 * ch + c >= kvalid) r[ch][c] = __float_as_uint(-INFINITY);
     }
     // row max on raw scores (the scale is positive), scaled once
-    float mx0 = __uint_as_float(r0[0]), mx1 = __uint_as_float(r1[0]);
+    float mxc[NC];
 #pragma unroll
-    for (int c = 1; c < 32; ++c) {
-      mx0 = fmaxf(mx0, __uint_as_float(r0[c]));
-      mx1 = fmaxf(mx1, __uint_as_float(r1[c]));
+    for (int ch = 0; ch < NC; ++ch) {
+      mxc[ch] = __uint_as_float(r[ch][0]);
+#pragma unroll
+      for (int c = 1; c < 32; ++c) mxc[ch] = fmaxf(mxc[ch], __uint_as_float(r[ch][c]));
     }
-    const float mx = fmaxf(mx0, mx1) * p.scale_log2;
+#pragma unroll
+    for (int ch = 1; ch < NC; ++ch) mxc[0] = fmaxf(mxc[0], mxc[ch]);
+    const float mx = mxc[0] * p.scale_log2;
     const float m_new = fmaxf(m, mx);
     const bool need = m_new > m + kLazy;  // always true on the first tile
     if (j > 0 && __any_sync(0xffffffffu, need)) {
@@ -172,22 +176,26 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
       l *= fast_exp2(m - m_new);
       m = m_new;
     }
-    // p = 2^(s * scale - m): one FMA and one exponential per score
-    uint32_t pk[32];
+    // p = 2^(s * scale - m): one FMA and one exponential per score; P_j
+    // (two 16-bit values per column) overwrites the first kBN/2 columns of S_j
     float2 acc2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const float a = fast_exp2(fmaf(__uint_as_float(r0[2 * c]), p.scale_log2, -m));
-      const float bb = fast_exp2(fmaf(__uint_as_float(r0[2 * c + 1]), p.scale_log2, -m));
-      const float x = fast_exp2(fmaf(__uint_as_float(r1[2 * c]), p.scale_log2, -m));
-      const float y = fast_exp2(fmaf(__uint_as_float(r1[2 * c + 1]), p.scale_log2, -m));
-      acc2 = add2(acc2, make_float2(a + x, bb + y));
-      pk[c] = pack_pair<T>(a, bb);
-      pk[16 + c] = pack_pair<T>(x, y);
+    for (int pc = 0; pc < NC / 2; ++pc) {
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float a = fast_exp2(fmaf(__uint_as_float(r[2 * pc][2 * c]), p.scale_log2, -m));
+        const float bb = fast_exp2(fmaf(__uint_as_float(r[2 * pc][2 * c + 1]), p.scale_log2, -m));
+        const float x = fast_exp2(fmaf(__uint_as_float(r[2 * pc + 1][2 * c]), p.scale_log2, -m));
+        const float y = fast_exp2(fmaf(__uint_as_float(r[2 * pc + 1][2 * c + 1]), p.scale_log2, -m));
+        acc2 = add2(acc2, make_float2(a + x, bb + y));
+        pk[c] = pack_pair<T>(a, bb);
+        pk[16 + c] = pack_pair<T>(x, y);
+      }
+      tmem_st32(tl + (j & 1) * kBN + 32 * pc, pk);
     }
     const float sum = acc2.x + acc2.y;
     l += sum;
-    tmem_st32(tl + (j & 1) * kBN, pk);  // P_j overwrites the first 32 columns of S_j
     tmem_wait_st();
     tc_fence_before();
     mbar_arrive(&p_full[j & 1]);
