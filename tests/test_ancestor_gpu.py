@@ -267,3 +267,24 @@ def test_cuda_graph_capture():
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("lens,d,H", [([511, 300, 130, 511, 64, 1], 8, 32), ([511, 511, 255, 400], 5, 32),
+                                      ([1023, 700, 129], 9, 4)])
+def test_deep_trees_ragged_subtree_tiles(lens, d, H):
+    # deep binary trees take the subtree tiling (tiles of sibling subtrees plus
+    # their root path); ragged lengths cut the last levels, and max_depth below
+    # the tree's depth truncates the walks (second case); with 32 heads the
+    # launch hands out (tile, head-chunk) units
+    b, D = 2, 64
+    g = torch.Generator().manual_seed(sum(lens) + d)
+    qs = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    ks = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    vs = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    O, L = ra.ragged_attention_with_lse(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    masks = [orc.ancestor_mask(n, b, d) for n in lens]
+    ref, rl = orc.padded_sdpa(qs, ks, vs, masks, return_lse=True)
+    err = (O.float().cpu() - torch.cat(ref, 0)).abs().max().item()
+    assert torch.allclose(O.float().cpu(), torch.cat(ref, 0), atol=ATOL, rtol=RTOL), f"peak_abs={err:.3e}"
+    assert torch.allclose(L.cpu(), torch.cat(rl, 0), atol=1e-3)
