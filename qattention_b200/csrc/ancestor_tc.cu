@@ -167,6 +167,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     it = items * blockIdx.x / gridDim.x;
     it_end = items * (blockIdx.x + 1) / gridDim.x;
   }
+  bool waited = false;  // griddepcontrol.wait done (before the first global read)
   while (it < it_end) {
   const int64_t tg = it / a.num_q_heads;
   const int h_first = int(it - tg * a.num_q_heads);
@@ -174,63 +175,161 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   it += h_end - h_first;
   const int tile = int(tg % p.geom.tiles);
   const int seq = int(tg / p.geom.tiles);
-  const int q0 = __ldg(a.cu_seqlens_q + seq);
-  const int len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
-  const int kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int wrow = warp * 16;  // first tile row of this warp
-  int q_lo = 0, nq = 0, wn = 0;
-  __syncthreads();  // the previous tile's plan is no longer read
+  const int g = lane >> 2, t = lane & 3;
+  // The plan depends on the tree shape only, not on the inputs: the first tile
+  // is planned for a full-length sequence before waiting for the previous
+  // kernel on the stream (programmatic dependent launch), so the planning
+  // overlaps that kernel's tail; it is redone if the sequence is shorter.
+  int q0 = 0, len = 0, kv0 = 0;
+  if (waited) {
+    q0 = __ldg(a.cu_seqlens_q + seq);
+    len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
+    kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
+  }
+  int len_plan = waited ? len : a.max_seqlen;
+  int q_lo = 0, nq = 0, wn = 0, nw = 0, nrows = 0, nkeys = 0, kpad = 0;
+  uint32_t sel0 = 0u, sel1 = 0u;  // walk-key masks, the same for every head
+  // token (relative to the sequence) of tile row r
+  auto row_tok = [&](int r) -> int {
+    if constexpr (SUB) return q_node[r];
+    else return q_lo + r;
+  };
+  // token of this thread's row g (half 0) or g + 8 (half 1), clamped to the
+  // warp's rows (the result is unused past them)
+  auto tok_g = [&](int half) -> int { return row_tok(wrow + min(g + 8 * half, max(wn - 1, 0))); };
+  for (;;) {
+  __syncthreads();  // the previous plan is no longer read
+  q_lo = 0;
+  wn = 0;
+  sel0 = sel1 = 0u;
+  nkeys = kpad = 0;
   if constexpr (SUB) {
     // ---- plans, shared by every head: the tile's staged windows (thread 1)
     // and each warp's key windows (lane 0 of each warp), computed in parallel ----
-    if (tid == 0) n_seg = tile_segments(p.geom, tile, len, seg_lo, seg_row);
+    if (tid == 0) n_seg = tile_segments(p.geom, tile, len_plan, seg_lo, seg_row);
     __syncthreads();
     nq = seg_row[n_seg];
-    if (nq == 0) continue;  // uniform over the CTA
-    wn = max(0, min(16, nq - wrow));
-    if (tid < nq) {
-      int i = 0;
-      while (seg_row[i + 1] <= tid) ++i;
-      q_node[tid] = seg_lo[i] + tid - seg_row[i];
+    if (nq > 0) {
+      wn = max(0, min(16, nq - wrow));
+      if (tid < nq) {
+        int i = 0;
+        while (seg_row[i + 1] <= tid) ++i;
+        q_node[tid] = seg_lo[i] + tid - seg_row[i];
+      }
+      if ((lane == 0 && wn > 0) || tid == 1) {
+        const bool cta = tid == 1;
+        int nwin = 0;
+        plan_rows(p.geom, seg_lo, seg_row, n_seg, cta ? 0 : wrow, cta ? nq : wrow + wn, a.max_depth,
+                  DevDivB{p.div_b}, cta ? win_lo : w_lo[warp], cta ? win_base : w_base[warp], nwin);
+        if (cta) n_win = nwin;
+        else w_nwin[warp] = nwin;
+      }
+      __syncthreads();
     }
-    if ((lane == 0 && wn > 0) || tid == 1) {
-      const bool cta = tid == 1;
-      int nwin = 0;
-      plan_rows(p.geom, seg_lo, seg_row, n_seg, cta ? 0 : wrow, cta ? nq : wrow + wn, a.max_depth,
-                DevDivB{p.div_b}, cta ? win_lo : w_lo[warp], cta ? win_base : w_base[warp], nwin);
-      if (cta) n_win = nwin;
-      else w_nwin[warp] = nwin;
-    }
-    __syncthreads();
   } else {
     // ---- contiguous tile: its walk levels are contiguous node ranges
     // (plan_levels_fit), for the CTA and for each warp's 16 rows ----
     q_lo = tile * kTcMQ;
-    if (q_lo >= len) continue;  // uniform over the CTA
-    nq = min(kTcMQ, len - q_lo);
-    wn = max(0, min(16, nq - wrow));
-    if (tid == 0) {
-      int ns = 0, nw = 0;
-      plan_levels_fit(q_lo, nq, a.max_depth, p.div_b, lv_off, win_lo, win_base, ns, nw);
-      n_win = nw;
+    nq = max(0, min(kTcMQ, len_plan - q_lo));
+    if (nq > 0) {
+      wn = max(0, min(16, nq - wrow));
+      if (tid == 0) {
+        int ns = 0, nwc = 0;
+        plan_levels_fit(q_lo, nq, a.max_depth, p.div_b, lv_off, win_lo, win_base, ns, nwc);
+        n_win = nwc;
+      }
+      if (lane == 0 && wn > 0 && warp > 0) {
+        int L = 0, nwin = 0;
+        plan_levels_fit(q_lo + wrow, wn, a.max_depth, p.div_b, w_col[warp], w_lo[warp], w_base[warp], L, nwin);
+        w_levels[warp] = L;
+        w_nwin[warp] = nwin;
+      }
+      if (tid == 32) {  // warp 0's plan, beside thread 0's
+        int L = 0, nwin = 0;
+        plan_levels_fit(q_lo, min(16, nq), a.max_depth, p.div_b, w_col[0], w_lo[0], w_base[0], L, nwin);
+        w_levels[0] = L;
+        w_nwin[0] = nwin;
+      }
+      __syncthreads();
     }
-    if (lane == 0 && wn > 0 && warp > 0) {
-      int L = 0, nwin = 0;
-      plan_levels_fit(q_lo + wrow, wn, a.max_depth, p.div_b, w_col[warp], w_lo[warp], w_base[warp], L, nwin);
-      w_levels[warp] = L;
-      w_nwin[warp] = nwin;
-    }
-    if (tid == 32) {  // warp 0's plan, beside thread 0's
-      int L = 0, nwin = 0;
-      plan_levels_fit(q_lo, min(16, nq), a.max_depth, p.div_b, w_col[0], w_lo[0], w_base[0], L, nwin);
-      w_levels[0] = L;
-      w_nwin[0] = nwin;
-    }
-    __syncthreads();
   }
-  const int nw = n_win, nrows = win_base[nw];
+  if (nq > 0) {
+    nw = n_win;
+    nrows = win_base[nw];
+    // key column -> staged slot (columns past the list repeat its last row)
+    nkeys = wn > 0 ? w_base[warp][w_nwin[warp]] : 0;
+    kpad = (nkeys + 15) & ~15;
+    if (wn > 0) {
+      const int nwin = w_nwin[warp];
+      for (int c = lane; c < kpad; c += 32) {
+        const int cc = min(c, nkeys - 1);
+        int wi = 0;
+        while (wi + 1 < nwin && w_base[warp][wi + 1] <= cc) ++wi;
+        const int node = w_lo[warp][wi] + (cc - w_base[warp][wi]);
+        int cw = 0;  // the CTA window that stages this node
+        while (cw + 1 < nw && node < win_lo[cw]) ++cw;  // windows descend in node order
+        kslot[warp][c] = win_base[cw] + node - win_lo[cw];
+      }
+    }
+    // ---- which fragment elements are this thread's rows' walk keys ----
+    // The thread owning column c of a row holds it in block c/8, element c%2
+    // when (c%8)/2 == t.
+    if constexpr (SUB) {
+      // row r's step-s key is the column of node_s(r) in the warp's windows (the
+      // walk descends, so the window index only grows)
+      if (wn > 0) {
+        const int* wl = w_lo[warp];
+        const int* wb = w_base[warp];
+        const int nwin = w_nwin[warp];
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          if (g + 8 * half >= wn) continue;
+          int n = tok_g(half), wi = 0;
+          uint32_t sel = 0u;
+          for (int s = 0; s <= a.max_depth; ++s) {
+            if (s > 0) {
+              if (n == 0) break;  // the walk ended at the root
+              n = int(fast_div(uint32_t(n - 1), p.div_b));
+            }
+            while (wi + 1 < nwin && n < wl[wi]) ++wi;
+            const int c = wb[wi] + n - wl[wi];
+            if (((c >> 1) & 3) == t) sel |= 1u << (((c >> 3) << 1) | (c & 1));
+          }
+          if (half) sel1 = sel; else sel0 = sel;
+        }
+      }
+    } else {
+      // row r's step-s key is column w_col[s] + node_s(r)
+      if (wn > 0) {
+        const int L = w_levels[warp];
+        const int* wc = w_col[warp];
+        int n0 = g < wn ? tok_g(0) : -1, n1 = g + 8 < wn ? tok_g(1) : -1;
+        for (int s = 0; s < L; ++s) {
+          if (s > 0) {
+            n0 = n0 <= 0 ? -1 : int(fast_div(uint32_t(n0 - 1), p.div_b));
+            n1 = n1 <= 0 ? -1 : int(fast_div(uint32_t(n1 - 1), p.div_b));
+          }
+          const int off = wc[s];
+          const int c0 = off + n0, c1 = off + n1;
+          if (n0 >= 0 && ((c0 >> 1) & 3) == t) sel0 |= 1u << (((c0 >> 3) << 1) | (c0 & 1));
+          if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
+        }
+      }
+    }
+  }
+  if (waited) break;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // inputs of the previous kernel are visible
+  waited = true;
+  q0 = __ldg(a.cu_seqlens_q + seq);
+  len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
+  kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
+  if (len == len_plan) break;
+  len_plan = len;  // a shorter sequence: plan again
+  }  // plan passes
+  if (nq == 0) continue;  // uniform over the CTA
   for (int j = tid; j < nrows; j += kTcThreads) {  // element offset of every staged row
     int w = 0;
     while (w + 1 < nw && win_base[w + 1] <= j) ++w;
@@ -238,79 +337,8 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     row_off[2 * j] = tk * a.k_stride_t * int64_t(sizeof(T));  // byte offsets
     row_off[2 * j + 1] = tk * a.v_stride_t * int64_t(sizeof(T));
   }
-  // token (relative to the sequence) of tile row r
-  auto row_tok = [&](int r) -> int {
-    if constexpr (SUB) return q_node[r];
-    else return q_lo + r;
-  };
-  // key column -> staged slot (columns past the list repeat its last row)
-  const int nkeys = wn > 0 ? w_base[warp][w_nwin[warp]] : 0;
-  const int kpad = (nkeys + 15) & ~15;
-  if (wn > 0) {
-    const int nwin = w_nwin[warp];
-    for (int c = lane; c < kpad; c += 32) {
-      const int cc = min(c, nkeys - 1);
-      int wi = 0;
-      while (wi + 1 < nwin && w_base[warp][wi + 1] <= cc) ++wi;
-      const int node = w_lo[warp][wi] + (cc - w_base[warp][wi]);
-      int cw = 0;  // the CTA window that stages this node
-      while (cw + 1 < nw && node < win_lo[cw]) ++cw;  // windows descend in node order
-      kslot[warp][c] = win_base[cw] + node - win_lo[cw];
-    }
-  }
-  const int g = lane >> 2, t = lane & 3;
   const int* ks = kslot[warp];
-  // token of this thread's row g (half 0) or g + 8 (half 1), clamped to the
-  // warp's rows (the result is unused past them)
-  auto tok_g = [&](int half) -> int { return row_tok(wrow + min(g + 8 * half, max(wn - 1, 0))); };
-  // ---- which fragment elements are this thread's rows' walk keys ----
-  // The thread owning column c of a row holds it in block c/8, element c%2
-  // when (c%8)/2 == t.
-  uint32_t sel0 = 0u, sel1 = 0u;  // same for every head
-  if constexpr (SUB) {
-    // row r's step-s key is the column of node_s(r) in the warp's windows (the
-    // walk descends, so the window index only grows)
-    if (wn > 0) {
-      const int* wl = w_lo[warp];
-      const int* wb = w_base[warp];
-      const int nwin = w_nwin[warp];
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        if (g + 8 * half >= wn) continue;
-        int n = tok_g(half), wi = 0;
-        uint32_t sel = 0u;
-        for (int s = 0; s <= a.max_depth; ++s) {
-          if (s > 0) {
-            if (n == 0) break;  // the walk ended at the root
-            n = int(fast_div(uint32_t(n - 1), p.div_b));
-          }
-          while (wi + 1 < nwin && n < wl[wi]) ++wi;
-          const int c = wb[wi] + n - wl[wi];
-          if (((c >> 1) & 3) == t) sel |= 1u << (((c >> 3) << 1) | (c & 1));
-        }
-        if (half) sel1 = sel; else sel0 = sel;
-      }
-    }
-    __syncthreads();  // row offsets are visible to every staging thread
-  } else {
-    // row r's step-s key is column w_col[s] + node_s(r)
-    if (wn > 0) {
-      const int L = w_levels[warp];
-      const int* wc = w_col[warp];
-      int n0 = g < wn ? tok_g(0) : -1, n1 = g + 8 < wn ? tok_g(1) : -1;
-      for (int s = 0; s < L; ++s) {
-        if (s > 0) {
-          n0 = n0 <= 0 ? -1 : int(fast_div(uint32_t(n0 - 1), p.div_b));
-          n1 = n1 <= 0 ? -1 : int(fast_div(uint32_t(n1 - 1), p.div_b));
-        }
-        const int off = wc[s];
-        const int c0 = off + n0, c1 = off + n1;
-        if (n0 >= 0 && ((c0 >> 1) & 3) == t) sel0 |= 1u << (((c0 >> 3) << 1) | (c0 & 1));
-        if (n1 >= 0 && ((c1 >> 1) & 3) == t) sel1 |= 1u << (((c1 >> 3) << 1) | (c1 & 1));
-      }
-    }
-    __syncthreads();  // row offsets are visible to every staging thread
-  }
+  __syncthreads();  // row offsets and key slots are visible to every thread
   // Staging: thread tid copies 16-byte chunk my_cc of rows my_r0, my_r0 + RPP,
   // ...; the swizzle term of those rows is my_x, flipped by kXStep per pass
   // (RPP is a multiple of 8, or 4 for head_dim 256).
@@ -592,9 +620,22 @@ int resident_ctas(int smem) {
   }
 }
 
+// Launched with programmatic stream serialisation: the kernel may start while
+// the previous kernel on the stream finishes; it plans its first tile, then
+// waits (griddepcontrol.wait) before its first read of any input.
 template <typename T, int D, int NBK, int MINB, bool SUB>
 int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st) {
-  ancestor_tc_kernel<T, D, NBK, MINB, SUB><<<dim3{unsigned(blocks)}, kTcThreads, smem, st>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(blocks));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, ancestor_tc_kernel<T, D, NBK, MINB, SUB>, p) != cudaSuccess) return QA_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
 
