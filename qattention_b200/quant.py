@@ -53,12 +53,90 @@ def quantize_w4a16(W: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     scales = (2.0 * amax / 15.0).to(torch.float16)              # [K/128, N]
     q = torch.round(Wf / scales.float()[:, None, :]) + 8.0
     q = q.clamp_(0, 15).to(torch.int32).reshape(K, N)           # [K, N] in 0..15
-    qt = q.t().contiguous().view(N, K // 8, 8)                  # [N, K/8, 8], k % 8 last
-    shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=W.device)
-    words = (qt.to(torch.int64) << shifts).sum(dim=-1)          # 0 .. 2^32-1
+    return pack_int4(q), scales.contiguous()
+
+
+def pack_int4(q: torch.Tensor) -> torch.Tensor:
+    """``[K, N]`` integer values in 0..15 -> this library's tile-major int32
+    ``[N/128, K/128, 4, 128, 4]`` packing (the inverse of :func:`unpack_int4`)."""
+    K, N = q.shape
+    if K % GROUP != 0 or N % 128 != 0:
+        raise ValueError(f"K ({K}) and N ({N}) must be multiples of 128")
+    qt = q.to(torch.int64).t().contiguous().view(N, K // 8, 8)  # [N, K/8, 8], k % 8 last
+    shifts = torch.tensor(NIBBLE_SHIFT, dtype=torch.int64, device=q.device)
+    words = (qt << shifts).sum(dim=-1)                          # 0 .. 2^32-1
     words = torch.where(words < 2**31, words, words - 2**32).to(torch.int32)  # [N, K/8]
-    qweight = words.view(N // 128, 128, K // 128, 4, 4).permute(0, 2, 3, 1, 4).contiguous()
-    return qweight, scales.contiguous()
+    return words.view(N // 128, 128, K // 128, 4, 4).permute(0, 2, 3, 1, 4).contiguous()
+
+
+def _unpack_gptq_nibbles(packed: torch.Tensor, along_rows: bool) -> torch.Tensor:
+    """GPTQ int32 packing, 8 values per word, value i in bits 4i..4i+3: rows
+    ``[R/8, C] -> [R, C]`` (``along_rows``) or columns ``[R, C/8] -> [R, C]``."""
+    w = packed.to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.arange(0, 32, 4, dtype=torch.int64, device=packed.device)
+    if along_rows:
+        vals = (w[:, None, :] >> shifts[None, :, None]) & 0xF   # [R/8, 8, C]
+        return vals.reshape(-1, packed.shape[1]).to(torch.int32)
+    vals = (w[:, :, None] >> shifts[None, None, :]) & 0xF       # [R, C/8, 8]
+    return vals.reshape(packed.shape[0], -1).to(torch.int32)
+
+
+def from_gptq(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor | None = None,
+              g_idx: torch.Tensor | None = None, *, group_size: int = GROUP,
+              zero_offset: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
+    """A GPTQ-format linear (the checkpoint layout GPTQModel / AutoGPTQ save and
+    the reference loads: scripts/w4a16_e2e.py:749-753, quantised with
+    bits=4, group_size=128, sym=True, desc_act=False at
+    scripts/quantize_llama31.py:41-46) -> ``(qweight, scales)`` in this
+    library's format, bit for bit the same weights.
+
+    GPTQ layout: ``qweight`` int32 ``[K/8, N]`` holds k = 8r + i of column n in
+    bits 4i..4i+3 of word ``[r, n]``; ``scales`` fp16 ``[K/group, N]``;
+    ``qzeros`` int32 ``[K/group, N/8]`` packs the zero points the same way
+    along N, stored minus ``zero_offset`` (1 in the classic checkpoint format,
+    0 in GPTQModel's internal one); ``g_idx`` int32 ``[K]`` is the group of each
+    k. Dequantisation is ``(q - zero) * scale`` in both formats, so a symmetric
+    checkpoint (every zero 8) with group 128 and no activation order maps onto
+    this library's ``fp16((q - 8) * scale)`` exactly. Anything else (asymmetric
+    zeros, another group size, an act-order ``g_idx``, bits other than 4)
+    raises ``ValueError``: the GEMM kernel implements that one format.
+    """
+    if qweight.dtype != torch.int32 or qweight.dim() != 2:
+        raise ValueError("qweight must be a 2-D int32 tensor [K/8, N] (4-bit GPTQ packing)")
+    K, N = qweight.shape[0] * 8, qweight.shape[1]
+    if group_size != GROUP:
+        raise ValueError(f"group_size {group_size} is not supported (the kernel uses {GROUP})")
+    if K % GROUP != 0 or N % 128 != 0:
+        raise ValueError(f"K ({K}) and N ({N}) must be multiples of 128")
+    if tuple(scales.shape) != (K // GROUP, N):
+        raise ValueError(f"scales must be [{K // GROUP}, {N}], got {tuple(scales.shape)}")
+    if g_idx is not None:
+        expect = torch.arange(K, device=g_idx.device, dtype=torch.int64) // GROUP
+        if g_idx.numel() != K or not torch.equal(g_idx.to(torch.int64).flatten(), expect):
+            raise ValueError("g_idx is not k // group_size: act-order (desc_act) checkpoints are not supported")
+    if qzeros is not None:
+        if tuple(qzeros.shape) != (K // GROUP, N // 8):
+            raise ValueError(f"qzeros must be [{K // GROUP}, {N // 8}], got {tuple(qzeros.shape)}")
+        zeros = _unpack_gptq_nibbles(qzeros, along_rows=False) + zero_offset
+        if not bool((zeros == 8).all()):
+            raise ValueError("asymmetric zero points: only symmetric (sym=True, zero 8) checkpoints are supported")
+    q = _unpack_gptq_nibbles(qweight, along_rows=True)          # [K, N] in 0..15
+    return pack_int4(q), scales.to(torch.float16).contiguous()
+
+
+def to_gptq(qweight: torch.Tensor, scales: torch.Tensor, zero_offset: int = 1):
+    """This library's ``(qweight, scales)`` -> GPTQ-format ``(qweight [K/8, N],
+    scales, qzeros [K/128, N/8], g_idx [K])`` (the inverse of :func:`from_gptq`)."""
+    q = unpack_int4(qweight).to(torch.int64)                   # [K, N]
+    K, N = q.shape
+    shifts = torch.arange(0, 32, 4, dtype=torch.int64, device=q.device)
+    words = (q.view(K // 8, 8, N) << shifts[None, :, None]).sum(dim=1)
+    gq = torch.where(words < 2**31, words, words - 2**32).to(torch.int32)
+    z = torch.full((K // GROUP, N // 8, 8), 8 - zero_offset, dtype=torch.int64, device=q.device)
+    zw = (z << shifts).sum(dim=-1)
+    qz = torch.where(zw < 2**31, zw, zw - 2**32).to(torch.int32)
+    g_idx = (torch.arange(K, device=q.device) // GROUP).to(torch.int32)
+    return gq, scales.contiguous(), qz, g_idx
 
 
 def unpack_int4(qweight: torch.Tensor) -> torch.Tensor:

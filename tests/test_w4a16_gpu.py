@@ -52,3 +52,20 @@ def test_gemm_strided_activations():
     Y = quant.w4a16_linear(X, qw.cuda(), sc.cuda())
     Y2 = quant.w4a16_linear(X.contiguous(), qw.cuda(), sc.cuda())
     assert torch.equal(Y, Y2)
+
+
+def test_gemm_on_gptq_checkpoint_tensors():
+    # a GPTQ-format linear (qweight [K/8, N], classic zero-1 qzeros, g_idx) loaded by
+    # quant.from_gptq runs through the GEMM like a natively quantised one
+    K, N, M = 1024, 384, 48
+    qw, sc = _weights(K, N, 21)
+    gq, gs, gz, gi = quant.to_gptq(qw, sc)
+    qw2, sc2 = quant.from_gptq(gq, gs, gz, gi)
+    g = torch.Generator().manual_seed(22)
+    X = torch.randn(M, K, generator=g).half()
+    Y = quant.w4a16_linear(X.cuda(), qw2.cuda(), sc2.cuda()).float().cpu()
+    q = quant.unpack_int4(qw2).numpy().astype(np.uint8)
+    ref = torch.from_numpy(wo.gemm(X.numpy(), q, sc2.numpy()))
+    scale = ref.abs().max().item() + 1e-6
+    assert (Y - ref).abs().max().item() <= 2e-3 * scale + 1e-3
+    assert torch.equal(qw2, qw) and torch.equal(sc2, sc)
