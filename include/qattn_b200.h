@@ -65,6 +65,12 @@ extern "C" {
  *              (src/ragged_attn.py:1576-1616); O and lse then describe the
  *              union of both key sets. prefix_o may alias o.
  */
+/* Paged K/V (replaces ragged_attention_paged, src/ragged_attn.py:827-1047): when
+ * page_table != NULL, K and V are caches [pages, page_size, kv_heads, D] and the KV row of
+ * sequence b's node n (plus kv_offset) is slot (n % page_size) of physical page
+ * page_table[b * page_table_stride + n / page_size]; k/v_stride_t are then the slot
+ * strides and k/v_stride_page the page strides (elements). Complete-tree mode only
+ * (parents == NULL, branching >= 2, head_dim 64/128/256); otherwise QA_ERR_UNSUPPORTED. */
 typedef struct qa_ancestor_args {
   const void* q;
   const void* k;
@@ -93,6 +99,10 @@ typedef struct qa_ancestor_args {
   int32_t max_seqlen;    /* >= longest sequence in cu_seqlens_q */
   float scale;           /* softmax scale, the reference uses 1/sqrt(D) */
   int32_t dtype;         /* QA_DTYPE_F16 / QA_DTYPE_BF16 */
+  const int32_t* page_table;    /* paged K/V: [batch, max_pages], device, optional */
+  int64_t page_table_stride;    /* elements between sequences' rows of page_table */
+  int64_t k_stride_page, v_stride_page;  /* paged K/V: elements between pages */
+  int32_t page_size;            /* paged K/V: tokens per page */
 } qa_ancestor_args;
 
 QA_API int qa_ancestor_attn(const qa_ancestor_args* args, void* stream);

@@ -9,9 +9,11 @@ built in-tree by ``python -m qattention_b200.build``.
 """
 from . import tree_mask  # noqa: F401
 from .ragged_attn import (  # noqa: F401
+    build_paged_kv,
     fused_lse_merge,
     pack_inputs,
     ragged_attention,
+    ragged_attention_paged,
     ragged_attention_sibling,
     ragged_attention_sibling_with_lse,
     ragged_attention_with_lse,

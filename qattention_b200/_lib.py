@@ -53,6 +53,8 @@ class AncestorArgs(Structure):
         ("head_dim", c_int32), ("kv_offset", c_int32), ("branching", c_int32),
         ("max_depth", c_int32), ("max_seqlen", c_int32),
         ("scale", c_float), ("dtype", c_int32),
+        ("page_table", c_void_p), ("page_table_stride", c_int64),
+        ("k_stride_page", c_int64), ("v_stride_page", c_int64), ("page_size", c_int32),
     ]
 
 

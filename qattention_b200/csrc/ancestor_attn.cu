@@ -357,8 +357,13 @@ extern "C" int qa_ancestor_attn(const qa_ancestor_args* args, void* stream) {
   p.tiles_per_seq = (a.max_seqlen + mq - 1) / mq;
   const bool parents = a.parents != nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (a.page_table != nullptr) {  // paged K/V: the tensor-core kernel only
+    if (a.page_size <= 0 || a.page_table_stride < 0 || a.parents != nullptr) return QA_ERR_INVALID;
+    if (!stride_ok(a.k_stride_page) || !stride_ok(a.v_stride_page)) return QA_ERR_ALIGN;
+  }
   const int tc = ancestor_tc_launch(a, st);
   if (tc != kTcNotApplicable) return tc;
+  if (a.page_table != nullptr) return QA_ERR_UNSUPPORTED;
   p.div_b = make_fast_div(uint32_t(parents ? 1 : a.branching));
   cudaError_t e = (a.dtype == QA_DTYPE_F16) ? launch_t<__half>(p, parents, st)
                                             : launch_t<__nv_bfloat16>(p, parents, st);

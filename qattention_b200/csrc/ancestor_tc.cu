@@ -330,12 +330,21 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   len_plan = len;  // a shorter sequence: plan again
   }  // plan passes
   if (nq == 0) continue;  // uniform over the CTA
-  for (int j = tid; j < nrows; j += kTcThreads) {  // element offset of every staged row
+  for (int j = tid; j < nrows; j += kTcThreads) {  // byte offset of every staged row
     int w = 0;
     while (w + 1 < nw && win_base[w + 1] <= j) ++w;
-    const int64_t tk = int64_t(kv0) + win_lo[w] + (j - win_base[w]);
-    row_off[2 * j] = tk * a.k_stride_t * int64_t(sizeof(T));  // byte offsets
-    row_off[2 * j + 1] = tk * a.v_stride_t * int64_t(sizeof(T));
+    const int node = win_lo[w] + (j - win_base[w]);
+    if (a.page_table == nullptr) {
+      const int64_t tk = int64_t(kv0) + node;
+      row_off[2 * j] = tk * a.k_stride_t * int64_t(sizeof(T));
+      row_off[2 * j + 1] = tk * a.v_stride_t * int64_t(sizeof(T));
+    } else {  // paged K/V: the row is a slot of the page the sequence's table names
+      const int pos = a.kv_offset + node;
+      const int64_t page = __ldg(a.page_table + int64_t(seq) * a.page_table_stride + pos / a.page_size);
+      const int slot = pos % a.page_size;
+      row_off[2 * j] = (page * a.k_stride_page + int64_t(slot) * a.k_stride_t) * int64_t(sizeof(T));
+      row_off[2 * j + 1] = (page * a.v_stride_page + int64_t(slot) * a.v_stride_t) * int64_t(sizeof(T));
+    }
   }
   const int* ks = kslot[warp];
   __syncthreads();  // row offsets and key slots are visible to every thread

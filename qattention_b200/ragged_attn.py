@@ -13,6 +13,8 @@ Reference entry points mirrored here (file:line in the reference project):
   ragged_attention_sibling(_with_lse) src/ragged_attn.py:1423-1556 (same math)
   fused_lse_merge                    src/ragged_attn.py:1619-1653
   ragged_attention_hybrid            src/ragged_attn.py:1851-1888
+  ragged_attention_paged             src/ragged_attn.py:827-1004
+  build_paged_kv                     src/ragged_attn.py:1007-1047
 """
 from __future__ import annotations
 
@@ -201,6 +203,87 @@ def ragged_attention_with_parents(
         raise ValueError(f"parents must have one entry per token ({Q.shape[0]}), got {parents.shape[0]}")
     par = parents.to(device=Q.device, dtype=torch.int32, non_blocking=True).contiguous()
     return _ancestor(Q, K, V, cu_dev, ms, parents=par, max_depth=max_depth, want_lse=True)
+
+
+def ragged_attention_paged(
+    Q: torch.Tensor,
+    K_cache: torch.Tensor,
+    V_cache: torch.Tensor,
+    page_table: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    branching_factor: int,
+    max_depth: int,
+) -> torch.Tensor:
+    """Ancestor-walk attention with a paged K/V cache (vLLM PagedAttention layout).
+
+    Q: packed ``[total_tokens, H, D]``; K_cache / V_cache: ``[pages, page_size, H_kv, D]``;
+    page_table: ``[B, max_pages]`` int32 (CPU or GPU), ``page_table[b, p]`` = physical page
+    of sequence b's logical page p; token n of sequence b (its BFS node n) is slot
+    ``n % page_size`` of page ``page_table[b, n // page_size]``. Returns O like ``Q``.
+    Mirrors src/ragged_attn.py:934-1004; the walk, the duplicate rule and the result
+    are those of :func:`ragged_attention`. The page lookup happens once per staged row
+    of a tile (not per walk step), in the tensor-core kernel.
+    """
+    assert K_cache.shape == V_cache.shape, "K and V cache shapes must match"
+    assert Q.dtype in _SUPPORTED and Q.dtype == K_cache.dtype == V_cache.dtype, (
+        f"Inputs must be fp16 or bf16 (got {Q.dtype})"
+    )
+    for name, t in (("Q", Q), ("K_cache", K_cache), ("V_cache", V_cache)):
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor: this library has no CPU path")
+    if Q.dim() != 3 or K_cache.dim() != 4:
+        raise ValueError("Q must be [tokens, heads, D] and the caches [pages, page_size, kv_heads, D]")
+    total, Hq, D = Q.shape
+    _, page_size, Hkv, Dk = K_cache.shape
+    if Dk != D or Hq % Hkv != 0:
+        raise ValueError(f"cache [.., {Hkv}, {Dk}] does not match Q [.., {Hq}, {D}]")
+    if branching_factor < 2:
+        raise ValueError("the paged walk needs branching_factor >= 2 (complete trees)")
+    if max_depth < 0:
+        raise ValueError(f"max_depth must be >= 0, got {max_depth}")
+    cu_dev, ms = _cu_and_max(cu_seqlens, None, Q.device)
+    pt = page_table.to(device=Q.device, dtype=torch.int32).contiguous()
+    Q, Kc, Vc = _rowable(Q), _rowable(K_cache), _rowable(V_cache)
+    O = torch.empty_like(Q, memory_format=torch.contiguous_format)
+    B = int(cu_dev.shape[0]) - 1
+    a = _lib.AncestorArgs()
+    a.q, a.k, a.v, a.o = Q.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr()
+    a.cu_seqlens_q = cu_dev.data_ptr()
+    a.q_stride_t, a.q_stride_h = Q.stride(0), Q.stride(1)
+    a.k_stride_t, a.k_stride_h, a.k_stride_page = Kc.stride(1), Kc.stride(2), Kc.stride(0)
+    a.v_stride_t, a.v_stride_h, a.v_stride_page = Vc.stride(1), Vc.stride(2), Vc.stride(0)
+    a.o_stride_t, a.o_stride_h = O.stride(0), O.stride(1)
+    a.page_table, a.page_table_stride, a.page_size = pt.data_ptr(), pt.stride(0), page_size
+    a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim = B, Hq, Hkv, D
+    a.branching, a.max_depth, a.max_seqlen = branching_factor, max_depth, ms
+    a.scale = 1.0 / math.sqrt(D)
+    a.dtype = _dtype_code(Q.dtype)
+    _lib.check(_lib.lib().qa_ancestor_attn(a, _stream_ptr(Q.device)), "qa_ancestor_attn (paged)")
+    return O
+
+
+def build_paged_kv(ks: List[torch.Tensor], vs: List[torch.Tensor], page_size: int = 16):
+    """Per-sequence K/V ``[L_b, H, D]`` -> ``(K_cache, V_cache, page_table)``: caches
+    ``[total_pages, page_size, H, D]`` (zero-padded last pages) on the inputs' device and
+    a CPU int32 ``[B, max_pages]`` table, sequence b's pages numbered consecutively after
+    those of sequences < b (src/ragged_attn.py:1007-1047)."""
+    B = len(ks)
+    H, D = ks[0].shape[1], ks[0].shape[2]
+    pages = [(k.shape[0] + page_size - 1) // page_size for k in ks]
+    total, max_pages = sum(pages), max(pages)
+    K_cache = torch.zeros(total, page_size, H, D, device=ks[0].device, dtype=ks[0].dtype)
+    V_cache = torch.zeros_like(K_cache)
+    page_table = torch.zeros(B, max_pages, dtype=torch.int32)
+    phys = 0
+    for b, (k, v) in enumerate(zip(ks, vs)):
+        L = k.shape[0]
+        for pg in range(pages[b]):
+            lo, hi = pg * page_size, min(pg * page_size + page_size, L)
+            K_cache[phys, : hi - lo] = k[lo:hi]
+            V_cache[phys, : hi - lo] = v[lo:hi]
+            page_table[b, pg] = phys
+            phys += 1
+    return K_cache, V_cache, page_table
 
 
 def ragged_attention_sibling(Q, K, V, cu_seqlens, branching_factor, max_depth, max_seqlen=None):

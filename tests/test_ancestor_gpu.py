@@ -288,3 +288,44 @@ def test_deep_trees_ragged_subtree_tiles(lens, d, H):
     err = (O.float().cpu() - torch.cat(ref, 0)).abs().max().item()
     assert torch.allclose(O.float().cpu(), torch.cat(ref, 0), atol=ATOL, rtol=RTOL), f"peak_abs={err:.3e}"
     assert torch.allclose(L.cpu(), torch.cat(rl, 0), atol=1e-3)
+
+
+@pytest.mark.parametrize("lens,b,d,H,Hkv,D,page", [
+    ([15, 9, 40, 15], 2, 3, 4, 4, 64, 16),          # contiguous tiles, ragged, truncated walks
+    ([1365, 1000, 1365], 4, 5, 8, 8, 128, 16),      # C2-shaped trees
+    ([511, 300, 130, 511], 2, 8, 8, 2, 64, 32),     # deep trees: subtree tiles, GQA
+])
+def test_paged_kv_matches_packed_and_oracle(lens, b, d, H, Hkv, D, page):
+    # src/ragged_attn.py:827-1047: K/V in pages through a page table; the physical
+    # pages are shuffled so the table matters. Same kernel as the packed path, so
+    # the outputs are bit-identical to ragged_attention on packed K/V.
+    g = torch.Generator().manual_seed(sum(lens) + page)
+    qs = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    ks = [torch.randn(n, Hkv, D, generator=g).half() for n in lens]
+    vs = [torch.randn(n, Hkv, D, generator=g).half() for n in lens]
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    Kc, Vc, pt = ra.build_paged_kv(ks, vs, page_size=page)
+    perm = torch.randperm(Kc.shape[0], generator=g)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(perm.numel())
+    Kc, Vc = Kc[perm], Vc[perm]                      # physical page j now holds old page perm[j]
+    pt = inv[pt.long()].to(torch.int32)
+    O = ra.ragged_attention_paged(Q.cuda(), Kc.cuda(), Vc.cuda(), pt, cu, b, d)
+    O_packed = ra.ragged_attention(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    assert torch.equal(O, O_packed)
+    rep = H // Hkv
+    masks = [orc.ancestor_mask(n, b, d) for n in lens]
+    ref = orc.padded_sdpa(qs, [k.repeat_interleave(rep, 1) for k in ks],
+                          [v.repeat_interleave(rep, 1) for v in vs], masks)
+    assert torch.allclose(O.float().cpu(), torch.cat(ref, 0), atol=ATOL, rtol=RTOL)
+
+
+def test_paged_kv_rejects_unsupported():
+    Q = torch.randn(15, 2, 64, device="cuda").half()
+    Kc = torch.zeros(1, 16, 2, 64, device="cuda").half()
+    pt = torch.zeros(1, 1, dtype=torch.int32)
+    cu = torch.tensor([0, 15], dtype=torch.int32)
+    with pytest.raises(ValueError):
+        ra.ragged_attention_paged(Q, Kc, Kc, pt, cu, 1, 3)       # chains are not paged
+    with pytest.raises(AssertionError):
+        ra.ragged_attention_paged(Q, Kc, Kc[:, :8], pt, cu, 2, 3)

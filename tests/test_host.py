@@ -114,4 +114,22 @@ def test_struct_layout_matches_header():
         types = {"const", "void", "float", "int32_t", "int64_t"}
         names += [t for t in re.split(r"[\s,*]+", line) if t and t not in types]
     assert names == [f[0] for f in _lib.AncestorArgs._fields_]
-    assert ctypes.sizeof(_lib.AncestorArgs) == 10 * 8 + 14 * 8 + 8 * 4 + 4 + 4
+    # 11 pointers and 17 int64 (8 bytes), 10 int32 and a float (4 bytes); the float and the
+    # int32 dtype pack into one 8-byte slot before the page-table pointer, page_size is
+    # padded to 8 at the end
+    assert ctypes.sizeof(_lib.AncestorArgs) == (11 + 17) * 8 + (10 + 1) * 4 + 4
+
+
+def test_build_paged_kv_layout():
+    # src/ragged_attn.py:1007-1047: consecutive physical pages per sequence, zero padding
+    from qattention_b200 import ragged_attn as ra
+    ks = [torch.arange(n * 2 * 8, dtype=torch.float32).view(n, 2, 8).half() for n in (5, 17, 16)]
+    vs = [k + 1 for k in ks]
+    Kc, Vc, pt = ra.build_paged_kv(ks, vs, page_size=8)
+    assert Kc.shape == (1 + 3 + 2, 8, 2, 8) and pt.dtype == torch.int32
+    assert pt.tolist() == [[0, 0, 0], [1, 2, 3], [4, 5, 0]]
+    for b, k in enumerate(ks):
+        for n in range(k.shape[0]):
+            assert torch.equal(Kc[pt[b, n // 8], n % 8], k[n])
+            assert torch.equal(Vc[pt[b, n // 8], n % 8], vs[b][n])
+    assert Kc[0, 5:].abs().sum() == 0
