@@ -556,31 +556,43 @@ def run_verify(args):
     for _ in range(max(args.warmup, 2)):
         model.step(tokens, cache, L, b, d)
     torch.cuda.synchronize(dev)
+    cur = torch.cuda.current_stream(dev)
+    # eager launches (for reference), then the step as one CUDA graph (VerifyModel.capture)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(steps):
+        model.step(tokens, cache, L, b, d)
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    eager_ms = _max_over_ranks(e0.elapsed_time(e1) / steps, ws)
+    graph, logits = model.capture(tokens, cache, L, b, d)
+    for _ in range(max(args.warmup, 2)):
+        graph.replay()
+    torch.cuda.synchronize(dev)
     clocks = ClockSampler(local)
     if rank == 0:
         clocks.start()
-    cur = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _barrier(ws)
     torch.cuda.synchronize(dev)
     clocks.mark("t0")
     e0.record(cur)
     for _ in range(steps):
-        model.step(tokens, cache, L, b, d)
+        graph.replay()
     e1.record(cur)
     torch.cuda.synchronize(dev)
     clocks.mark("t1")
     ms = _max_over_ranks(e0.elapsed_time(e1) / steps, ws)
     if rank == 0:
         clocks.stop()
-    # end to end: tokens H2D from pinned memory, the step, argmax tokens D2H
+    # end to end: tokens H2D from pinned memory into the graph's input, the step, argmax tokens D2H
     out_host = torch.empty(B * N, dtype=torch.int64).pin_memory()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _barrier(ws)
     f0.record(cur)
     for _ in range(steps):
-        t = tok_host.to(dev, non_blocking=True)
-        out_host.copy_(model.step(t, cache, L, b, d).argmax(-1), non_blocking=True)
+        tokens.copy_(tok_host, non_blocking=True)
+        graph.replay()
+        out_host.copy_(logits.argmax(-1), non_blocking=True)
     f1.record(cur)
     torch.cuda.synchronize(dev)
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1) / steps, ws)
@@ -598,6 +610,7 @@ def run_verify(args):
                    "sequences_per_gpu": B, "parallelism": f"sequences sharded over {ws} GPU(s), no collective"},
         "e2e": {"value": tokens_total / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": B * N * 8, "d2h_bytes_per_step": B * N * 8},
+        "eager_ms_per_step": eager_ms, "timing": "one CUDA graph per step (VerifyModel.capture); eager launches beside",
         "clocks": clocks.summary()}), flush=True)
 
 

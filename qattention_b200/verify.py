@@ -101,6 +101,7 @@ class VerifyModel:
         self.norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=self.dev)).half()
         self.lm_head = (torch.randn(H, cfg.vocab, generator=g, device=self.dev) * std).half()
         self.inv_freq = llama31_inv_freq(cfg).to(self.dev)
+        self._pos = {}  # (prefix_len, branching, depth, B) -> int32 positions on the device
 
     def new_cache(self, batch: int, prefix_len: int, tree_len: int, seed: int = 1):
         """Per-layer K/V caches [B, Hkv, L+N, D]: the prefix filled (as after a prefill)."""
@@ -129,7 +130,11 @@ class VerifyModel:
         H, D, Hq, Hkv, F = c.hidden, c.head_dim, c.heads, c.kv_heads, c.ffn
         L = _lib.lib()
         st = torch.cuda.current_stream(self.dev).cuda_stream
-        pos = (prefix_len + tree_depths(branching, depth)).to(self.dev, torch.int32).repeat(B)
+        key = (prefix_len, branching, depth, B)
+        pos = self._pos.get(key)
+        if pos is None:  # made once, outside any graph capture (a host-to-device copy)
+            pos = (prefix_len + tree_depths(branching, depth)).to(self.dev, torch.int32).repeat(B)
+            self._pos[key] = pos
         h = self.embed[tokens.reshape(-1)]                       # residual stream [M, H]
         x = torch.empty(M, H, dtype=torch.float16, device=self.dev)
         qkv = torch.empty(M, (Hq + 2 * Hkv) * D, dtype=torch.float16, device=self.dev)
@@ -159,3 +164,20 @@ class VerifyModel:
         _lib.check(L.qa_add_rmsnorm(h.data_ptr(), delta.data_ptr(), self.norm.data_ptr(), x.data_ptr(), M, H,
                                     c.rms_eps, st), "qa_add_rmsnorm")
         return x @ self.lm_head
+
+    def capture(self, tokens: torch.Tensor, cache, prefix_len: int, branching: int, depth: int):
+        """Record one verify step in a CUDA graph (the reference captures its verify
+        forward too: scripts/w4a16_e2e.py:1455-1575). ``tokens`` is the static input
+        buffer (copy new tokens into it before a replay); returns ``(graph, logits)``
+        where ``logits`` is the static output. Every launch of the step (GEMMs,
+        attention, elementwise kernels, the LM head) is in the graph; the first call
+        runs the step eagerly on a side stream to create its buffers and memos."""
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):
+            self.step(tokens, cache, prefix_len, branching, depth)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits = self.step(tokens, cache, prefix_len, branching, depth)
+        return graph, logits

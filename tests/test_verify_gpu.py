@@ -118,3 +118,24 @@ def test_add_rmsnorm_and_silu_mul():
     assert (out.float() - ref).abs().max() < 2e-2 * ref.abs().max()
     a_ref = torch.nn.functional.silu(gu[:, :F].float()) * gu[:, F:].float()
     assert (act.float() - a_ref).abs().max() < 1e-2 * a_ref.abs().max() + 1e-3
+
+
+def test_verify_step_cuda_graph_replay_matches_eager():
+    # the whole verify step (every layer's GEMMs, attention and elementwise kernels
+    # plus the LM head) captured once and replayed with new tokens
+    cfg = vf.LlamaConfig(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000)
+    model = vf.VerifyModel(cfg, "cuda", seed=11, std=0.05)
+    b, d, L, B = 2, 4, 96, 2
+    N = (b ** (d + 1) - 1) // (b - 1)
+    cache = model.new_cache(B, L, N, seed=12)
+    tokens = torch.zeros(B, N, dtype=torch.int64, device="cuda")
+    graph, logits = model.capture(tokens, cache, L, b, d)
+    gen = torch.Generator().manual_seed(13)
+    for _ in range(2):
+        new = torch.randint(0, cfg.vocab, (B, N), generator=gen).cuda()
+        tokens.copy_(new)
+        graph.replay()
+        torch.cuda.synchronize()
+        eager = model.step(new, cache, L, b, d)
+        assert torch.equal(logits, eager)
+    assert _lib.device_error() == 0
