@@ -1,15 +1,18 @@
 // Ancestor-walk attention, complete-tree mode, on tensor cores (mma.sync).
 //
 // Same result as the scalar walk in ancestor_attn.cu (and as the reference's
-// _ragged_attn_sparse_kernel(_lse), src/ragged_attn.py:267-496), organised so
-// that per-query overhead disappears:
-//   * Work item = (sequence, tile of 64 consecutive BFS queries, query head);
-//     a persistent grid (one CTA per resident slot) takes equal contiguous
-//     ranges of the items, tile-major, and plans each tile once for all of its
-//     heads.
-//   * Plan: at walk level s the ancestors of a contiguous query range are a
-//     contiguous node range (ancestor_plan.cuh); the tile's levels merge into
-//     windows of K/V rows that are staged in shared memory once per head.
+// _ragged_attn_sparse_kernel(_lse), src/ragged_attn.py:267-496, and its paged
+// variant, :827-1004), organised so that per-query overhead disappears:
+//   * Work item = (sequence, tile of <= 64 queries, query head). Tiles are
+//     64 consecutive BFS nodes, or (deep trees) sibling subtrees cut from
+//     bands of levels plus their root path (ancestor_plan.cuh), whichever
+//     stages fewer rows. A persistent grid (one CTA per resident slot) takes
+//     equal contiguous ranges of the items, tile-major, or one (tile, head
+//     chunk) unit per CTA when that balances better; a tile is planned once
+//     for all of its heads.
+//   * Plan: the walk keys of a tile's rows form a few windows of consecutive
+//     nodes (ancestor_plan.cuh); their K/V rows are staged in shared memory
+//     once per head (through a page table when K/V are paged).
 //   * A warp owns 16 queries; their keys over all levels form one key list
 //     (<= 128 columns). S = Q . K_list^T runs as mma.sync m16n8k16 (fp32
 //     accumulate) with S kept in registers; a per-thread bitmask (built once
@@ -17,14 +20,18 @@
 //     max over the walk) sees the reference's key set. P is normalised, rounded
 //     to fp16 (bf16: hi + lo split) and reused from the S registers as the A
 //     operand of O = P . V_list.
+//   * The head loop is software-pipelined with two cp.async groups per head
+//     (next head's Q/K during this head's P.V and epilogue, its V during its
+//     own S and softmax).
 //   * Tensor cores here only cut instruction count: the pass is a gather bound
 //     by HBM bandwidth (~2.8 flop per byte).
 //   * Shared rows use a 16-byte-chunk XOR swizzle (chunk ^ (row & 7)), unrolled
 //     into the ldmatrix/stmatrix addresses, so row reads are bank-conflict
 //     free; the output tile leaves through stmatrix and 16-byte streaming
 //     stores.
-// Used when every walk level of a tile fits in shared memory (always true for
-// b >= 2; chains up to depth ~300), for head_dim 64, 128 and 256.
+// Used for branching >= 2 when a tile's rows and a warp's key list fit (the
+// host plans every tile's capacity), for head_dim 64, 128 and 256; chains and
+// explicit parents take the scalar walk.
 #include <atomic>
 #include <mutex>
 
