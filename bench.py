@@ -1,6 +1,6 @@
 """Benchmark of the tree-verification hot path (one JSON line on rank 0).
 
-Workload (N=1 headline): BASELINE config 2 — B=8 complete 4-ary trees of depth
+Workload (N=1 headline): bench config C2 — B=8 complete 4-ary trees of depth
 5 (N=1365 tokens each, 10920 packed), H=32, D=128, fp16, no prefix. One step =
 one ancestor-walk attention pass over the batch (``ragged_attention_with_lse``
 semantics, O and LSE written). ``--config C3`` selects config 3 (B=16 binary
@@ -19,7 +19,7 @@ masked SDPA, restated in oracle/, all host threads) on a bounded sample.
 
 Secondary arms (one JSON line each, N=1; used for the profiles of the other
 hot-path kernels, not the headline):
-``--kernel prefix``  BASELINE config 4's shared-prefix pass (B=16, L=10240 prefix
+``--kernel prefix``  bench config C4's shared-prefix pass (B=16, L=10240 prefix
                      keys, 341 tree queries, GQA 32/8, D=128): TFLOP/s against
                      the measured bf16 tensor peak.
 ``--kernel verify``  config 5: the W4A16 tree-verify step of random-init

@@ -214,7 +214,7 @@ QA_API int qa_w4a16_dequant(const int32_t* qweight, const void* scales, void* ou
                             void* stream);
 
 /*
- * Elementwise steps of the W4A16 verify step (the Llama
+ * Elementwise steps of the W4A16 verify step (bench config C5; the Llama
  * decoder-layer code the reference runs around its attention,
  * scripts/w4a16_e2e.py:1393-1431). fp16 tensors, fp32 arithmetic, 16-byte
  * aligned, contiguous rows.

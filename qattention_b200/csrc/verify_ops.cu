@@ -1,4 +1,4 @@
-// Elementwise kernels of the W4A16 verify step: the work
+// Elementwise kernels of the W4A16 verify step (bench config C5): the work
 // between the GEMMs and the attention of one Llama decoder layer, each fused
 // so that it reads and writes its tensors once.
 //

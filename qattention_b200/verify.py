@@ -1,4 +1,4 @@
-"""W4A16 tree-verify step of a Llama-architecture model on this package's kernels.
+"""W4A16 tree-verify step of a Llama-architecture model (bench config C5) on this package's kernels.
 
 The reference's end-to-end script (scripts/w4a16_e2e.py) runs EAGLE-3 tree
 verification on a GPTQ-int4 Llama-3.1-8B: every decoder layer projects the

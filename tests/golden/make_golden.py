@@ -13,7 +13,7 @@ stores their outputs with the inputs that produced them:
   verify_tree_mask results for a set of (b, d) and seeds.
 * ``pack_inputs.npz``    — cu_seqlens of pack_inputs for ragged lengths.
 * ``sdpa_cases.npz``     — padded masked SDPA outputs (the reference oracle,
-  fp16 output as the reference casts it) for BASELINE config 1 (fp32 inputs,
+  fp16 output as the reference casts it) for bench config C1 (fp32 inputs,
   seed 0) and a sample of the reference test sweep's shapes (fp16 inputs).
 """
 from __future__ import annotations
@@ -73,7 +73,7 @@ def main(ref_root: str) -> None:
     np.savez_compressed(HERE / "pack_inputs.npz", **packs)
 
     cases = {}
-    # one binary tree b=2 d=3 (N=15), H=4, D=64, fp32 N(0,1) from seed 0,
+    # bench config C1: one binary tree b=2 d=3 (N=15), H=4, D=64, fp32 N(0,1) from seed 0,
     # drawn in the order q, k, v.
     g = torch.Generator().manual_seed(0)
     N = tm.num_tree_nodes(2, 3)
@@ -103,4 +103,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the reference checkout>")
+    main(sys.argv[1])

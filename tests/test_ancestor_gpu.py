@@ -91,7 +91,7 @@ def test_golden_fixtures(golden, case):
 
 
 def test_config1_fp32_inputs(golden):
-    # BASELINE config 1 draws fp32 inputs; the kernel computes from their fp16 cast.
+    # bench config C1 draws fp32 inputs; the kernel computes from their fp16 cast.
     c = golden["sdpa_cases"]
     q, k, v = (torch.from_numpy(c[f"c1_{x}"]) for x in "qkv")
     cu = torch.tensor([0, q.shape[0]], dtype=torch.int32)
@@ -232,7 +232,7 @@ def test_batch_permutation_is_bit_exact():
 
 @pytest.mark.parametrize("cfg", ["C2", "C3"])
 def test_full_size_sliced_against_oracle(cfg):
-    # BASELINE configs 2 and 3 at full size; the oracle checks the first and last tree
+    # bench configs C2 and C3 at full size; the oracle checks the first and last tree
     B, b, d = (8, 4, 5) if cfg == "C2" else (16, 2, 9)
     H, D = 32, 128
     N = tm.num_tree_nodes(b, d)

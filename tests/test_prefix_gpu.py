@@ -118,7 +118,7 @@ def test_tree_verify_attention_e2e_layout(use_parents):
 
 
 def test_config4_full_size_first_sequence():
-    """B=16, L=10240, 4-ary depth-4 trees (N=341), GQA 32/8, D=128."""
+    """bench config C4: B=16, L=10240, 4-ary depth-4 trees (N=341), GQA 32/8, D=128."""
     B, L, b, d, Hq, Hkv, D = 16, 10240, 4, 4, 32, 8, 128
     N = tm.num_tree_nodes(b, d)
     g = torch.Generator().manual_seed(4)
