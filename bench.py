@@ -1,43 +1,40 @@
 """Benchmark of the tree-verification hot path (one JSON line on rank 0).
 
-Workload (N=1 headline): bench config C2 — B=8 complete 4-ary trees of depth
-5 (N=1365 tokens each, 10920 packed), H=32, D=128, fp16, no prefix. One step =
-one ancestor-walk attention pass over the batch (``ragged_attention_with_lse``
-semantics, O and LSE written). ``--config C3`` selects config 3 (B=16 binary
-trees of depth 9).
+Headline workload: bench config C3 — B=16 complete binary trees of depth 9
+(N=1023 tokens each, 16368 packed), H=32, D=128, fp16, no prefix, sharded by
+tree across the ranks (strong scaling: the global batch is fixed, rank r owns
+16/N trees through ``qattention_b200.sharding``). One step = one ancestor-walk
+attention pass (``ragged_attention_with_lse`` semantics, O and LSE written)
+over the rank's trees.
 
-value  = algorithmic HBM bytes of all ranks' steps / device time (GB/s), where
-         algorithmic bytes = Q, K, V read once + O written once + LSE (4 B/row).
-e2e    = the same metric through the public API with pinned host buffers:
-         H2D of Q/K/V, the call, D2H of O and LSE inside the timed region.
-Multi-GPU (torchrun): each rank runs its own batch of the workload (trees are
-independent; weak scaling); no collective inside the timed region; one NCCL
-all-gather of per-rank checksums afterwards.
+value  = algorithmic HBM bytes of the whole batch / device time of the slowest
+         rank (GB/s), where algorithmic bytes = Q, K, V read once + O written
+         once + LSE (4 B/row).
+e2e    = the same metric through the public API (sharding helper ->
+         ``ragged_attention_with_lse``) with pinned host buffers: each rank's
+         H2D of its Q/K/V, the call, D2H of its O and LSE inside the timed region.
+After timing, O and LSE are gathered to rank 0 with one NCCL gather per tensor
+(timed under ``gather``) and checked against the CPU oracle on two trees.
+
+Secondary results in the same line (``secondary``): config C2 (B=8 4-ary trees
+of depth 5) sharded the same way; at N=1 also the reference's Triton kernel on
+C2 and C3 (``triton_reference``, imported unmodified from ``baseline/_ref`` where
+it is installed), config C4 whole verify attention and its prefix pass beside
+the reference's prefix phase (``repeat_kv`` + aten flash SDPA), the W4A16
+layer sweep at M = 16, 64, 1023, 8184; at every N config C5's W4A16 verify step
+(8 sequences split over the ranks).
 
 ``--impl reference`` times the reference's CPU path for this operator (padded
 masked SDPA, restated in oracle/, all host threads) on a bounded sample.
 
-Secondary arms (one JSON line each, N=1; used for the profiles of the other
-hot-path kernels, not the headline):
-``--kernel prefix``  bench config C4's shared-prefix pass (B=16, L=10240 prefix
-                     keys, 341 tree queries, GQA 32/8, D=128): TFLOP/s against
-                     the measured bf16 tensor peak.
-``--kernel verify``  config 5: the W4A16 tree-verify step of random-init
-                     Llama-3.1-8B (32 layers) on B=8 sequences (2048-token prefix
-                     + binary depth-9 tree), tokens/s; under torchrun the 8
-                     sequences are split over the ranks (strong scaling).
-``--kernel hybrid``  config 4 whole: prefix pass + ancestor pass with the LSE
-                     merge fused (``tree_verify_attention``), µs per call.
-``--kernel w4a16``   the W4A16 linears of one Llama-3.1-8B decoder layer (q/k/v
-                     and gate/up fused along N: 4 GEMMs)
-                     (config 5's architecture, random-init int4 weights) at
-                     M = 16, 64, 1023 and 8184 tokens; value = weight-stream
-                     GB/s at M = 64 (HBM-bound regime), the sweep in ``sweep``.
+Stand-alone arms (one JSON line each, N=1): ``--kernel prefix | hybrid |
+w4a16 | verify`` print the same secondary measurements as their own lines.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -56,7 +53,9 @@ CONFIGS = {
     "C2": (8, 4, 5, 32, 128),
     "C3": (16, 2, 9, 32, 128),
 }
+HEADLINE = "C3"
 L2_BYTES = 126 * 1024 * 1024
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
 def _num_nodes(b: int, d: int) -> int:
@@ -75,6 +74,14 @@ def _peaks():
             j = json.load(f)
         return float(j["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def _tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 class ClockSampler:
@@ -164,18 +171,36 @@ def _max_over_ranks(x: float, ws: int) -> float:
     return float(t.item())
 
 
-def make_inputs(cfg: str, seed: int):
-    """Seeded synthetic fp16 N(0,1) inputs on the host: packed Q, K, V and cu_seqlens."""
+def make_trees(cfg: str, lo: int, hi: int, seed: int = 0):
+    """Seeded synthetic fp16 N(0,1) inputs of trees lo..hi-1 of a config, on the host.
+
+    Each tree has its own generator (seed, tree index), so a tree's values do not
+    depend on how the batch is sharded. Returns packed Q, K, V and cu_seqlens.
+    """
     B, b, d, H, D = CONFIGS[cfg]
     N = _num_nodes(b, d)
-    g = torch.Generator().manual_seed(seed)
-    Q, K, V = (torch.randn(B * N, H, D, generator=g, dtype=torch.float32).half() for _ in range(3))
-    cu = torch.arange(0, (B + 1) * N, N, dtype=torch.int32)
-    return Q, K, V, cu, (B, b, d, H, D, N)
+    qs, ks, vs = [], [], []
+    for t in range(lo, hi):
+        g = torch.Generator().manual_seed(seed * 100003 + t)
+        qs.append(torch.randn(N, H, D, generator=g).half())
+        ks.append(torch.randn(N, H, D, generator=g).half())
+        vs.append(torch.randn(N, H, D, generator=g).half())
+    n = hi - lo
+    if n == 0:
+        e = torch.empty(0, H, D, dtype=torch.float16)
+        return e, e.clone(), e.clone(), torch.zeros(1, dtype=torch.int32)
+    cu = torch.arange(0, (n + 1) * N, N, dtype=torch.int32)
+    return torch.cat(qs), torch.cat(ks), torch.cat(vs), cu
+
+
+def global_cu(cfg: str) -> torch.Tensor:
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    return torch.arange(0, (B + 1) * N, N, dtype=torch.int32)
 
 
 def _traffic_from_profile(cfg: str):
-    """DRAM bytes per launch of the ancestor kernel from the committed ncu summary, if any."""
+    """DRAM bytes per full-batch launch of the ancestor kernel from the committed ncu summary, if any."""
     p = os.path.join(ROOT, "profiles", "ancestor_attn_traffic.json")
     if not os.path.exists(p):
         return None
@@ -184,78 +209,77 @@ def _traffic_from_profile(cfg: str):
     return j.get(cfg, {}).get("dram_bytes_per_launch")
 
 
-def cpu_reference_step(Q, K, V, shape, heads: int, trees: int = 1):
-    """The reference's CPU path on a sample: padded masked SDPA over `trees` trees × `heads` heads."""
-    from oracle import tree_attn_oracle as orc
-    B, b, d, H, D, N = shape
-    mask = orc.ancestor_mask(N, b, d)
-    qs = [Q[i * N:(i + 1) * N, :heads] for i in range(trees)]
-    ks = [K[i * N:(i + 1) * N, :heads] for i in range(trees)]
-    vs = [V[i * N:(i + 1) * N, :heads] for i in range(trees)]
-    return orc.padded_sdpa(qs, ks, vs, [mask] * trees)
+def graph_steps(fn, copies: int, dev, per_graph: int = 8):
+    """CUDA graphs of back-to-back steps over rotating input copies.
+
+    One graph of G steps (G a multiple of `copies`; consecutive launches overlap
+    through programmatic dependent launch, as in a serving loop) plus one
+    single-step graph per copy for a remainder; returns run(n), which replays
+    exactly n steps.
+    """
+    G = copies * max(1, per_graph // copies)
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for i in range(copies):
+            fn(i)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    graph_g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_g):
+        for j in range(G):
+            fn(j)
+    singles = []
+    for i in range(copies):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn(i)
+        singles.append(g)
+
+    def run(n):
+        for _ in range(n // G):
+            graph_g.replay()
+        for i in range(n % G):
+            singles[i % copies].replay()
+
+    run.graphs = (graph_g, singles)
+    run.per_graph = G
+    return run
 
 
-def cpu_sample_plan(Q, K, V, shape, per_step_budget_s: float):
-    """Pick how many heads of one tree a CPU step covers so it fits the budget."""
-    B, b, d, H, D, N = shape
-    t0 = time.perf_counter()
-    cpu_reference_step(Q, K, V, shape, 1)
-    t1 = time.perf_counter() - t0
-    heads = int(max(1, min(H, per_step_budget_s // max(t1, 1e-6))))
-    return heads
+def time_run(run, steps: int, warmup: int, dev, before=None, after=None) -> float:
+    """ms per step of run(n) with CUDA events on the current stream.
+
+    `before` runs after the warm-up and a synchronize, right before the first
+    event (a barrier, a clock mark); `after` right after the closing synchronize.
+    """
+    run(warmup)
+    torch.cuda.synchronize(dev)
+    if before is not None:
+        before()
+        torch.cuda.synchronize(dev)
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    run(steps)
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    if after is not None:
+        after()
+    return e0.elapsed_time(e1) / steps
 
 
-def run_reference(args):
-    """--impl reference: the reference's CPU implementation of the path (oracle restatement)."""
-    ws, rank, _ = _dist()
-    if rank != 0:
-        return
-    torch.set_num_threads(os.cpu_count() or 1)
-    Q, K, V, cu, shape = make_inputs(args.config, 0)
-    B, b, d, H, D, N = shape
-    heads = cpu_sample_plan(Q, K, V, shape, 150.0 / max(1, args.steps + args.warmup))
-    for _ in range(args.warmup):
-        cpu_reference_step(Q, K, V, shape, heads)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu_reference_step(Q, K, V, shape, heads)
-    dt = (time.perf_counter() - t0) / args.steps
-    nbytes = algorithmic_bytes(N, heads, D)
-    gbs = nbytes / dt / 1e9
-    sample = f"1 of {B} trees x {heads} of {H} heads per step (padded masked SDPA, fp32, torch CPU)"
-    line = {
-        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": _config_dict(args.config, shape),
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+def _rotating(Qh, Kh, Vh, dev, nbytes):
+    copies = max(2, -(-3 * L2_BYTES // max(nbytes, 1)))
+    return copies, [(Qh.to(dev), Kh.to(dev), Vh.to(dev)) for _ in range(copies)]
 
 
-def _config_dict(cfg, shape):
-    B, b, d, H, D, N = shape
-    return {"workload": f"{cfg}: B={B} complete {b}-ary trees depth {d} (N={N}/tree, T={B * N}), "
-                        f"H={H}, D={D}, fp16 I/O, no prefix",
-            "batch": B, "branching": b, "depth": d, "heads": H, "head_dim": D, "tokens": B * N,
-            "parallelism": "trees sharded per rank (weak scaling)",
-            "l2": "rotating input copies, total > 3x the 126 MB L2"}
-
-
-def run_ours(args):
+def time_ancestor_ours(cfg, Qh, Kh, Vh, cu, dev, steps, warmup, before=None, after=None):
+    """Device ms per step of this library's ancestor pass (graph replay, rotating copies)."""
     from qattention_b200 import ragged_attn as ra
-
-    ws, rank, local = _dist()
-    dev = torch.device("cuda", local)
-    Qh, Kh, Vh, cu, shape = make_inputs(args.config, 1000 * rank)
-    B, b, d, H, D, N = shape
-    T = B * N
-    nbytes = algorithmic_bytes(T, H, D)
-    in_bytes = 3 * T * H * D * 2
-    copies = max(2, -(-3 * L2_BYTES // nbytes))
-    ins = [(Qh.to(dev), Kh.to(dev), Vh.to(dev)) for _ in range(copies)]
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    T = Qh.shape[0]
+    copies, ins = _rotating(Qh, Kh, Vh, dev, algorithmic_bytes(T, H, D))
     cud = cu.to(dev)
     O = torch.empty(T, H, D, dtype=torch.float16, device=dev)
     L = torch.empty(T, H, dtype=torch.float32, device=dev)
@@ -264,145 +288,67 @@ def run_ours(args):
         Q, K, V = ins[i % copies]
         ra._ancestor(Q, K, V, cud, N, branching=b, max_depth=d, want_lse=True, out=O, lse_out=L)
 
-    # CUDA graphs of back-to-back steps over the rotating input copies: one of G steps
-    # (the kernel is launched with programmatic dependent launch, so a step plans its
-    # first tile while the previous step finishes, as consecutive launches of a serving
-    # loop do; each step still waits for the previous one before touching memory) and
-    # one single-step graph per copy for a remainder, so that exactly K steps run
-    G = copies * max(1, 8 // copies)
-    stream = torch.cuda.Stream(dev)
-    stream.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(stream):
-        for i in range(copies):
-            step(i)
-    torch.cuda.current_stream(dev).wait_stream(stream)
-    graph_g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph_g):
-        for j in range(G):
-            step(j)
-    graphs = []
-    for i in range(copies):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            step(i)
-        graphs.append(g)
-
-    def run(n):  # exactly n steps
-        for _ in range(n // G):
-            graph_g.replay()
-        for i in range(n % G):
-            graphs[i % copies].replay()
-
-    run(args.warmup)
+    run = graph_steps(step, copies, dev)
+    ms = time_run(run, steps, warmup, dev, before, after)
+    step(0)
     torch.cuda.synchronize(dev)
-
-    clocks = ClockSampler(local)
-    if rank == 0:
-        clocks.start()
-    cur = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    _barrier(ws)
-    torch.cuda.synchronize(dev)
-    clocks.mark("t0")
-    e0.record(cur)
-    run(args.steps)
-    e1.record(cur)
-    torch.cuda.synchronize(dev)
-    clocks.mark("t1")
-    _barrier(ws)
-    ms = e0.elapsed_time(e1) / args.steps
-    ms_max = _max_over_ranks(ms, ws)
-    if rank == 0:
-        clocks.stop()
-
-    # end to end through the public API: pinned host inputs, H2D + call + D2H in the timed region
-    Qp, Kp, Vp = Qh.pin_memory(), Kh.pin_memory(), Vh.pin_memory()
-    Op = torch.empty(T, H, D, dtype=torch.float16).pin_memory()
-    Lp = torch.empty(T, H, dtype=torch.float32).pin_memory()
-    e2e_steps = max(3, min(args.steps, 20))
-
-    def e2e_step():
-        Qd, Kd, Vd = (x.to(dev, non_blocking=True) for x in (Qp, Kp, Vp))
-        Od, Ld = ra.ragged_attention_with_lse(Qd, Kd, Vd, cu, b, d)
-        Op.copy_(Od, non_blocking=True)
-        Lp.copy_(Ld, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    _barrier(ws)
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(cur)
-    for _ in range(e2e_steps):
-        e2e_step()
-    f1.record(cur)
-    torch.cuda.synchronize(dev)
-    e2e_ms = _max_over_ranks(f0.elapsed_time(f1) / e2e_steps, ws)
-
-    # the only collective: gather per-rank output checksums to every rank (after timing)
-    csum = torch.stack([O.float().sum(), L.sum()]).double()
-    if ws > 1:
-        import torch.distributed as dist
-        gathered = [torch.zeros_like(csum) for _ in range(ws)]
-        dist.all_gather(gathered, csum)
-    if rank != 0:
-        return
-
-    peak, peak_kind = _peaks()
-    gbs = nbytes * ws / (ms_max * 1e-3) / 1e9
-    per_gpu_gbs = nbytes / (ms * 1e-3) / 1e9
-    cpu_base = None
-    if ws == 1 and not args.skip_cpu:
-        torch.set_num_threads(os.cpu_count() or 1)
-        heads = cpu_sample_plan(Qh, Kh, Vh, shape, 2.0)
-        t0 = time.perf_counter()
-        n = 0
-        while True:
-            cpu_reference_step(Qh, Kh, Vh, shape, heads)
-            n += 1
-            if time.perf_counter() - t0 > args.cpu_seconds:
-                break
-        cdt = (time.perf_counter() - t0) / n
-        cpu_base = {"value": algorithmic_bytes(N, heads, D) / cdt / 1e9, "unit": "GB/s",
-                    "cores": torch.get_num_threads(), "kind": "port",
-                    "sample": f"{n} runs x 1 of {B} trees x {heads} of {H} heads "
-                              "(padded masked SDPA, fp32, torch CPU)"}
-    traffic = _traffic_from_profile(args.config)
-    line = {
-        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_max, "us_per_step": ms_max * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic", "config": {**_config_dict(args.config, shape),
-                                        "graphs": f"{G} back-to-back steps per CUDA graph over the rotating copies "
-                                                  "(programmatic dependent launch between steps)"},
-        "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
-                     "frac": per_gpu_gbs / peak, "peak_kind": peak_kind,
-                     "traffic": traffic, "algorithmic_bytes": nbytes,
-                     "kernel": "ancestor_tc_kernel (qa_ancestor_attn)"},
-        "cpu_baseline": cpu_base,
-        "e2e": {"value": nbytes * ws / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
-                "ms_per_step": e2e_ms, "h2d_bytes_per_step": in_bytes,
-                "d2h_bytes_per_step": T * H * D * 2 + T * H * 4},
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-        "checksum": [float(x) for x in csum.tolist()],
-    }
-    print(json.dumps(line), flush=True)
+    del run
+    return ms, O, L, copies
 
 
-def _timed_graphs(graphs, steps, warmup, dev):
-    """Replays the captured graphs round-robin; returns ms per replay (CUDA events)."""
-    for i in range(warmup):
-        graphs[i % len(graphs)].replay()
-    torch.cuda.synchronize(dev)
-    cur = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(cur)
-    for i in range(steps):
-        graphs[i % len(graphs)].replay()
-    e1.record(cur)
-    torch.cuda.synchronize(dev)
-    return e0.elapsed_time(e1) / steps
+def _import_reference():
+    """The unmodified reference module from baseline/_ref (None, reason when absent)."""
+    if not os.path.isdir(os.path.join(REF_DIR, "src")):
+        return None, "baseline/_ref is not installed (the reference package was not found next to bench.py)"
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import src.ragged_attn as ref  # noqa: WPS433 (the reference's own module name)
+        return ref, None
+    except Exception as e:  # the reason goes into the JSON line
+        return None, f"import failed: {type(e).__name__}: {str(e).splitlines()[0][:200]}"
+
+
+def time_triton_reference(cfg, dev, steps, warmup, ours_out=None, seed=0):
+    """The reference's Triton kernel (``ragged_attention_with_lse``) on the same inputs and timing.
+
+    Its first calls run its autotuner; the timed steps replay CUDA graphs over the
+    same rotating input copies as this library's arm. Returns a dict for the
+    JSON line (``unavailable`` with the reason when it cannot run).
+    """
+    ref, why = _import_reference()
+    if ref is None:
+        return {"unavailable": why}
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    Qh, Kh, Vh, cu = make_trees(cfg, 0, B, seed)
+    T = Qh.shape[0]
+    nbytes = algorithmic_bytes(T, H, D)
+    try:
+        copies, ins = _rotating(Qh, Kh, Vh, dev, nbytes)
+        cud = cu.to(dev)
+        for i in range(copies):  # autotune outside the graphs
+            ref.ragged_attention_with_lse(*ins[i], cud, b, d, max_seqlen=N)
+        torch.cuda.synchronize(dev)
+        outs = {}
+
+        def step(i):
+            outs["o"] = ref.ragged_attention_with_lse(*ins[i % copies], cud, b, d, max_seqlen=N)
+
+        run = graph_steps(step, copies, dev)
+        ms = time_run(run, steps, warmup, dev)
+        O, L = ref.ragged_attention_with_lse(*ins[0], cud, b, d, max_seqlen=N)
+        torch.cuda.synchronize(dev)
+        res = {"us_per_step": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
+               "kernel": "_ragged_attn_sparse_kernel_lse (Triton, reference src/ragged_attn.py:401-572)",
+               "timing": "CUDA-graph replay of back-to-back steps over the same rotating copies"}
+        if ours_out is not None:
+            res["max_abs_diff_vs_ours"] = float((O.float() - ours_out[0].float()).abs().max())
+            res["lse_max_abs_diff_vs_ours"] = float((L - ours_out[1]).abs().max())
+        del run, ins
+        return res
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200] if str(e) else ''}"}
 
 
 def _capture(fn, n, dev):
@@ -421,82 +367,98 @@ def _capture(fn, n, dev):
     return graphs
 
 
-def _tensor_peak():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(p):
-        with open(p) as f:
-            return float(json.load(f)["bf16_tflops"]), "measured"
-    return 1590.0, "fallback"
+def _timed_graphs(graphs, steps, warmup, dev):
+    """Replays the captured graphs round-robin; returns ms per replay (CUDA events)."""
+    def run(n):
+        for i in range(n):
+            graphs[i % len(graphs)].replay()
+    return time_run(run, steps, warmup, dev)
 
 
-def run_prefix(args):
-    """Shared-prefix pass of config 4 (tcgen05 kernel), TFLOP/s."""
+C4 = dict(B=16, L=10240, b=4, d=4, Hq=32, Hkv=8, D=128)
+
+
+def measure_prefix(dev, steps, warmup):
+    """Config 4's shared-prefix pass: this library's tcgen05 kernel, and the reference's
+    prefix phase on the same inputs (``repeat_kv`` then aten flash SDPA,
+    scripts/w4a16_e2e.py:1236-1249), both timed by graph replay."""
     from qattention_b200 import ragged_attn as ra
-    dev = torch.device("cuda", 0)
-    B, L, N, Hq, Hkv, D = 16, 10240, 341, 32, 8, 128
+    B, L, Hq, Hkv, D = C4["B"], C4["L"], C4["Hq"], C4["Hkv"], C4["D"]
+    N = _num_nodes(C4["b"], C4["d"])
     g = torch.Generator().manual_seed(4)
     Q = torch.randn(B, N, Hq, D, generator=g).half().to(dev)
     K = torch.randn(B, L, Hkv, D, generator=g).half().to(dev)
     V = torch.randn(B, L, Hkv, D, generator=g).half().to(dev)
-    graphs = _capture(lambda i: ra.prefix_attention_with_lse(Q, K, V), 1, dev)
-    clocks = ClockSampler(0)
-    clocks.start()
-    clocks.mark("t0")
-    ms = _timed_graphs(graphs, args.steps, args.warmup, dev)
-    clocks.mark("t1")
-    clocks.stop()
     flops = 4.0 * B * Hq * N * L * D
-    tf = flops / (ms * 1e-3) / 1e12
+    graphs = _capture(lambda i: ra.prefix_attention_with_lse(Q, K, V), 1, dev)
+    ms = _timed_graphs(graphs, steps, warmup, dev)
+    O, LSE = ra.prefix_attention_with_lse(Q, K, V)
+    del graphs
     peak, kind = _tensor_peak()
-    print(json.dumps({
-        "metric": "prefix pass TFLOP/s", "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "f16",
-        "data": "synthetic", "config": {"workload": "C4 prefix pass: B=16, L=10240 prefix keys, N=341 tree "
-                                        "queries, GQA 32/8, D=128, fp16", "l2": "K/V 671 MB > L2"},
-        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
-                     "peak_kind": kind, "flops_per_launch": flops, "kernel": "prefix_attn_kernel (qa_prefix_attn)"},
-        "gpu_launches": args.steps, "clocks": clocks.summary()}), flush=True)
+    res = {"us": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12, "peak": peak, "peak_kind": kind,
+           "frac": flops / (ms * 1e-3) / 1e12 / peak, "flops_per_launch": flops,
+           "kernel": "prefix_attn_kernel (qa_prefix_attn)"}
+    # the reference's prefix phase: K/V in the model's [B, H, L, D] layout after repeat_kv
+    Qr = Q.transpose(1, 2).contiguous()
+    Kc, Vc = K.transpose(1, 2).contiguous(), V.transpose(1, 2).contiguous()  # [B, Hkv, L, D] cache
+
+    def repeat_kv(x):
+        return x[:, :, None].expand(B, Hkv, Hq // Hkv, L, D).reshape(B, Hq, L, D)
+
+    def ref_phase(_):
+        Kr, Vr = repeat_kv(Kc).contiguous(), repeat_kv(Vc).contiguous()
+        return torch.ops.aten._scaled_dot_product_flash_attention(
+            Qr, Kr, Vr, dropout_p=0.0, is_causal=False, scale=1.0 / math.sqrt(D), return_debug_mask=False)
+
+    try:
+        out = ref_phase(0)
+        ref_o = out[0].transpose(1, 2).float()
+        diff = float((ref_o - O.float()).abs().max())
+        graphs = _capture(ref_phase, 1, dev)
+        ms_ref = _timed_graphs(graphs, steps, warmup, dev)
+        del graphs
+        Kr, Vr = repeat_kv(Kc).contiguous(), repeat_kv(Vc).contiguous()
+        lib_graphs = _capture(lambda i: torch.ops.aten._scaled_dot_product_flash_attention(
+            Qr, Kr, Vr, dropout_p=0.0, is_causal=False, scale=1.0 / math.sqrt(D), return_debug_mask=False), 1, dev)
+        ms_flash = _timed_graphs(lib_graphs, steps, warmup, dev)
+        del lib_graphs, Kr, Vr
+        res["reference_prefix_phase"] = {
+            "us": ms_ref * 1e3, "tflops": flops / (ms_ref * 1e-3) / 1e12,
+            "flash_alone_us": ms_flash * 1e3, "flash_alone_tflops": flops / (ms_flash * 1e-3) / 1e12,
+            "what": "repeat_kv of the [B, Hkv, L, D] cache + aten _scaled_dot_product_flash_attention "
+                    "(scripts/w4a16_e2e.py:1236-1249); flash_alone = the SDPA call on pre-expanded K/V",
+            "max_abs_diff_vs_ours": diff}
+    except Exception as e:
+        res["reference_prefix_phase"] = {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    return res
 
 
-# (name, K, N) of one Llama-3.1-8B decoder layer, Y = X W with W [K, N]; q/k/v
-# and gate/up are fused along N as serving stacks load them (same weights, 4 GEMMs)
-def run_hybrid(args):
+def measure_hybrid(dev, steps, warmup):
     """Config 4 whole verify attention: tcgen05 prefix pass + ancestor pass with the LSE merge fused."""
     from qattention_b200 import ragged_attn as ra
-    dev = torch.device("cuda", 0)
-    B, L, b, d, Hq, Hkv, D = 16, 10240, 4, 4, 32, 8, 128
+    B, L, b, d, Hq, Hkv, D = (C4[k] for k in ("B", "L", "b", "d", "Hq", "Hkv", "D"))
     N = _num_nodes(b, d)
     g = torch.Generator().manual_seed(6)
     Q = torch.randn(B, Hq, N, D, generator=g).half().to(dev)
     K = torch.randn(B, Hkv, L + N, D, generator=g).half().to(dev)
     V = torch.randn(B, Hkv, L + N, D, generator=g).half().to(dev)
     graphs = _capture(lambda i: ra.tree_verify_attention(Q, K, V, b, d), 1, dev)
-    clocks = ClockSampler(0)
-    clocks.start()
-    clocks.mark("t0")
-    ms = _timed_graphs(graphs, args.steps, args.warmup, dev)
-    clocks.mark("t1")
-    clocks.stop()
+    ms = _timed_graphs(graphs, steps, warmup, dev)
+    del graphs
     prefix_flops = 4.0 * B * Hq * N * L * D
-    print(json.dumps({
-        "metric": "tree-verify attention us (prefix + tree, merged)", "value": ms * 1e3, "unit": "us",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
-        "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "C4: B=16, L=10240 cached prefix + complete 4-ary depth-4 tree (N=341), "
-                               "GQA 32/8, D=128; ragged_attention tree_verify_attention (KV cache layout "
-                               "[B, Hkv, L+N, D], no repeat_kv)", "l2": "K/V 2.1 GB > L2"},
-        "prefix_tflops": prefix_flops / (ms * 1e-3) / 1e12,
-        "gpu_launches": args.steps * 2, "clocks": clocks.summary()}), flush=True)
+    return {"us": ms * 1e3, "prefix_tflops_of_whole": prefix_flops / (ms * 1e-3) / 1e12,
+            "what": "tree_verify_attention on the [B, Hkv, L+N, D] KV cache (no repeat_kv)"}
 
 
+# (name, K, N) of one Llama-3.1-8B decoder layer, Y = X W with W [K, N]; q/k/v
+# and gate/up are fused along N as serving stacks load them (same weights, 4 GEMMs)
 LLAMA_LINEARS = [("qkv", 4096, 6144), ("o", 4096, 4096), ("gate_up", 4096, 28672), ("down", 14336, 4096)]
 
 
-def run_w4a16(args):
+def measure_w4a16(dev, steps, warmup, ms_list):
     """One decoder layer's W4A16 linears (random-init int4 weights) at several M."""
     import ctypes
     from qattention_b200 import _lib, quant
-    dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(5)
     layer = []
     for _, K, N in LLAMA_LINEARS:
@@ -505,21 +467,18 @@ def run_w4a16(args):
     wbytes = sum(qw.numel() * 4 + sc.numel() * 2 for qw, sc, _, _ in layer)
     copies = max(2, -(-3 * L2_BYTES // wbytes))
     layers = [layer] + [[(qw.clone(), sc.clone(), K, N) for qw, sc, K, N in layer] for _ in range(copies - 1)]
-    clocks = ClockSampler(0)
-    clocks.start()
-    clocks.mark("t0")
     sweep = {}
-    for M in [int(m) for m in args.w4_m.split(",")]:
+    for M in ms_list:
         xs = {K: torch.randn(M, K, device=dev).half() for K in (4096, 14336)}
         ys = [torch.empty(M, N, dtype=torch.float16, device=dev) for _, _, _, N in layer]
 
-        def step(i, M=M, xs=xs, ys=ys):
+        def step(i, xs=xs, ys=ys):
             for j, (qw, sc, K, N) in enumerate(layers[i % copies]):
                 quant.w4a16_linear(xs[K], qw, sc, out=ys[j])
 
         graphs = _capture(step, copies, dev)
-        steps = max(copies, min(args.steps, 200 if M <= 1023 else 40))
-        ms = _timed_graphs(graphs, steps, args.warmup, dev)
+        n = max(copies, min(steps, 200 if M <= 1023 else 40))
+        ms = _timed_graphs(graphs, n, warmup, dev)
         flops = sum(2.0 * M * K * N for _, _, K, N in layer)
         launches = 0
         for _, _, K, N in layer:  # one GEMM, plus the split-K reduce when the plan splits K
@@ -529,51 +488,38 @@ def run_w4a16(args):
         sweep[str(M)] = {"us_per_layer": ms * 1e3, "weight_gbs": wbytes / (ms * 1e-3) / 1e9,
                          "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_layer": launches}
         del graphs
-    clocks.mark("t1")
-    clocks.stop()
     hb, hkind = _peaks()
     tp, tkind = _tensor_peak()
-    m_small = "64" if "64" in sweep else min(sweep, key=int)
-    m_large = max(sweep, key=int)
-    v = sweep[m_small]["weight_gbs"]
-    print(json.dumps({
-        "metric": f"W4A16 weight-stream GB/s (M={m_small})", "value": v, "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sweep[m_small]["us_per_layer"] * 1e-3,
-        "higher_is_better": True, "dtype": "int4 x f16 -> f32 acc", "data": "synthetic (random-init weights)",
-        "config": {"workload": "Llama-3.1-8B decoder layer W4A16 linears, qkv and gate_up fused "
-                                "(4 GEMMs, 218.1 M weights, group 128)",
-                   "l2": f"{copies} rotating weight copies (> 3x L2)"},
-        "roofline": {"bound": "hbm", "achieved": v, "peak": hb, "unit": "GB/s", "frac": v / hb, "peak_kind": hkind,
-                     "bytes_per_layer": wbytes, "kernel": "w4a16_gemm_kernel (qa_w4a16_gemm)"},
-        "large_m_roofline": {"bound": "tensor", "M": int(m_large), "achieved": sweep[m_large]["tflops"], "peak": tp,
-                             "unit": "TFLOP/s", "frac": sweep[m_large]["tflops"] / tp, "peak_kind": tkind},
-        "sweep": sweep, "clocks": clocks.summary()}), flush=True)
+    for v in sweep.values():
+        v["hbm_frac"] = v["weight_gbs"] / hb
+        v["tensor_frac"] = v["tflops"] / tp
+    return {"sweep": sweep, "bytes_per_layer": wbytes, "copies": copies, "hbm_peak": hb, "hbm_peak_kind": hkind,
+            "tensor_peak": tp, "tensor_peak_kind": tkind,
+            "workload": "Llama-3.1-8B decoder layer W4A16 linears, qkv and gate_up fused (4 GEMMs, 218.1 M "
+                        "weights, group 128), rotating weight copies > 3x L2"}
 
 
-def run_verify(args):
-    """Config 5: W4A16 tree-verify step of random-init Llama-3.1-8B, tokens/s (strong scaling over ranks)."""
+def measure_verify(ws, rank, dev, steps, warmup, layers=0):
+    """Config 5: the W4A16 tree-verify step, 8 sequences split over the ranks; tokens/s (strong scaling)."""
     from qattention_b200 import verify as vf
-    ws, rank, local = _dist()
-    dev = torch.device("cuda", local)
     B_all, L, b, d = 8, 2048, 2, 9
     if B_all % ws:
-        raise SystemExit("config 5 shards 8 sequences: use 1, 2, 4 or 8 GPUs")
+        return {"unavailable": "config 5 shards 8 sequences: use 1, 2, 4 or 8 GPUs"}
     B = B_all // ws
     N = _num_nodes(b, d)
     cfg = vf.LlamaConfig()
-    if args.verify_layers:
-        cfg.layers = args.verify_layers
+    if layers:
+        cfg.layers = layers
     model = vf.VerifyModel(cfg, dev, seed=7)
     cache = model.new_cache(B, L, N, seed=8 + rank)
     g = torch.Generator().manual_seed(9 + rank)
     tok_host = torch.randint(0, cfg.vocab, (B, N), generator=g).pin_memory()
     tokens = tok_host.to(dev)
-    steps = max(1, min(args.steps, 10))
-    for _ in range(max(args.warmup, 2)):
+    steps = max(1, min(steps, 10))
+    for _ in range(max(warmup, 2)):
         model.step(tokens, cache, L, b, d)
     torch.cuda.synchronize(dev)
     cur = torch.cuda.current_stream(dev)
-    # eager launches (for reference), then the step as one CUDA graph (VerifyModel.capture)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(cur)
     for _ in range(steps):
@@ -582,25 +528,17 @@ def run_verify(args):
     torch.cuda.synchronize(dev)
     eager_ms = _max_over_ranks(e0.elapsed_time(e1) / steps, ws)
     graph, logits = model.capture(tokens, cache, L, b, d)
-    for _ in range(max(args.warmup, 2)):
+    for _ in range(max(warmup, 2)):
         graph.replay()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(local)
-    if rank == 0:
-        clocks.start()
     _barrier(ws)
     torch.cuda.synchronize(dev)
-    clocks.mark("t0")
     e0.record(cur)
     for _ in range(steps):
         graph.replay()
     e1.record(cur)
     torch.cuda.synchronize(dev)
-    clocks.mark("t1")
     ms = _max_over_ranks(e0.elapsed_time(e1) / steps, ws)
-    if rank == 0:
-        clocks.stop()
-    # end to end: tokens H2D from pinned memory into the graph's input, the step, argmax tokens D2H
     out_host = torch.empty(B * N, dtype=torch.int64).pin_memory()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _barrier(ws)
@@ -612,22 +550,292 @@ def run_verify(args):
     f1.record(cur)
     torch.cuda.synchronize(dev)
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1) / steps, ws)
+    del graph, logits, model, cache
+    torch.cuda.empty_cache()
+    tokens_total = B_all * N
+    return {"tokens_per_s": tokens_total / (ms * 1e-3), "ms_per_step": ms, "eager_ms_per_step": eager_ms,
+            "e2e": {"tokens_per_s": tokens_total / (e2e_ms * 1e-3), "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": B * N * 8, "d2h_bytes_per_step": B * N * 8},
+            "layers": cfg.layers, "sequences_per_gpu": B, "steps": steps,
+            "workload": f"C5: random-init Llama-3.1-8B architecture ({cfg.layers} layers), W4A16 linears "
+                        "(qkv and gate_up fused), fp16 LM head; B=8 sequences x (2048-token cached prefix + "
+                        "binary depth-9 tree, 1023 tokens) = 8184 verify tokens per step, sharded by sequence",
+            "timing": "one CUDA graph per step (VerifyModel.capture), max over ranks"}
+
+
+def cpu_reference_step(Q, K, V, cfg, heads: int, trees: int = 1):
+    """The reference's CPU path on a sample: padded masked SDPA over `trees` trees x `heads` heads."""
+    from oracle import tree_attn_oracle as orc
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    mask = orc.ancestor_mask(N, b, d)
+    qs = [Q[i * N:(i + 1) * N, :heads] for i in range(trees)]
+    ks = [K[i * N:(i + 1) * N, :heads] for i in range(trees)]
+    vs = [V[i * N:(i + 1) * N, :heads] for i in range(trees)]
+    return orc.padded_sdpa(qs, ks, vs, [mask] * trees)
+
+
+def cpu_sample_plan(Q, K, V, cfg, per_step_budget_s: float):
+    """How many heads of one tree a CPU step covers so that it fits the budget."""
+    H = CONFIGS[cfg][3]
+    t0 = time.perf_counter()
+    cpu_reference_step(Q, K, V, cfg, 1)
+    t1 = time.perf_counter() - t0
+    return int(max(1, min(H, per_step_budget_s // max(t1, 1e-6))))
+
+
+def _config_dict(cfg, ws):
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    return {"workload": f"{cfg}: B={B} complete {b}-ary trees depth {d} (N={N}/tree, T={B * N}), "
+                        f"H={H}, D={D}, fp16 I/O, no prefix",
+            "batch": B, "branching": b, "depth": d, "heads": H, "head_dim": D, "tokens": B * N,
+            "parallelism": f"trees sharded by qattention_b200.sharding over {ws} rank(s) (strong scaling: "
+                           f"{B // ws if B % ws == 0 else 'about ' + str(B / ws)} trees per GPU), no collective "
+                           "in the timed region, one NCCL gather of O and LSE afterwards",
+            "l2": "rotating input copies, total > 3x the 126 MB L2"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU implementation of the path (oracle restatement), rank 0 only."""
+    ws, rank, _ = _dist()
     if rank != 0:
         return
-    tokens_total = B_all * N
-    print(json.dumps({
-        "metric": "W4A16 verify-step tokens/s", "value": tokens_total / (ms * 1e-3), "unit": "tokens/s",
-        "n_gpus": ws, "steps": steps, "warmup": max(args.warmup, 2), "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int4 weights x f16 activations, f32 accumulate", "data": "synthetic (random-init weights, random tokens)",
-        "config": {"workload": f"C5: random-init Llama-3.1-8B architecture ({cfg.layers} layers), W4A16 linears "
-                               "(qkv and gate_up fused), fp16 LM head; B=8 sequences x (2048-token cached prefix "
-                               "+ binary depth-9 tree, 1023 tokens) = 8184 verify tokens per step",
-                   "sequences_per_gpu": B, "parallelism": f"sequences sharded over {ws} GPU(s), no collective"},
-        "e2e": {"value": tokens_total / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": B * N * 8, "d2h_bytes_per_step": B * N * 8},
-        "eager_ms_per_step": eager_ms, "timing": "one CUDA graph per step (VerifyModel.capture); eager launches beside",
-        "clocks": clocks.summary()}), flush=True)
+    cfg = args.config
+    torch.set_num_threads(os.cpu_count() or 1)
+    Q, K, V, cu = make_trees(cfg, 0, 1, 0)
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    heads = cpu_sample_plan(Q, K, V, cfg, 150.0 / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        cpu_reference_step(Q, K, V, cfg, heads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference_step(Q, K, V, cfg, heads)
+    dt = (time.perf_counter() - t0) / args.steps
+    gbs = algorithmic_bytes(N, heads, D) / dt / 1e9
+    sample = (f"1 of {B} trees x {heads} of {H} heads per step (padded masked SDPA, fp32, torch CPU); "
+              "GB/s from that sample's own algorithmic bytes")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": _config_dict(cfg, args.gpus),
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _oracle_check(O, L, cfg, trees, heads=8, seed=0):
+    """Max |O - oracle| and |LSE - oracle| over the given trees (first `heads` heads)."""
+    from oracle import tree_attn_oracle as orc
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    eo = el = 0.0
+    for t in trees:
+        Q, K, V, cu = make_trees(cfg, t, t + 1, seed)
+        ref, rl = orc.sparse_ancestor_attention(Q[:, :heads], K[:, :heads], V[:, :heads], cu, b, d)
+        s = slice(t * N, (t + 1) * N)
+        eo = max(eo, float((O[s, :heads].float() - ref.float()).abs().max()))
+        el = max(el, float((L[s, :heads].double() - rl).abs().max()))
+    return eo, el
+
+
+def ancestor_sharded(cfg, ws, rank, dev, steps, warmup, clocks=None, with_e2e=True, with_gather=True):
+    """Config `cfg` sharded by tree over the ranks: device time, e2e, gather, oracle check."""
+    from qattention_b200 import sharding
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    sh = sharding.shard_trees(global_cu(cfg), ws, rank)
+    Qh, Kh, Vh, cu = make_trees(cfg, sh.tree_lo, sh.tree_hi, 0)
+    local_bytes = algorithmic_bytes(sh.num_tokens, H, D)
+    total_bytes = algorithmic_bytes(B * N, H, D)
+
+    def before():
+        _barrier(ws)
+        if clocks is not None:
+            clocks.mark("t0")
+
+    def after():
+        if clocks is not None:
+            clocks.mark("t1")
+        _barrier(ws)
+
+    ms, O, L, copies = time_ancestor_ours(cfg, Qh, Kh, Vh, cu, dev, steps, warmup, before, after)
+    ms_max = _max_over_ranks(ms, ws)
+    res = {"ms_per_step": ms_max, "us_per_step": ms_max * 1e3, "local_us": ms * 1e3,
+           "gbs": total_bytes / (ms_max * 1e-3) / 1e9, "per_gpu_gbs": local_bytes / (ms * 1e-3) / 1e9,
+           "local_bytes": local_bytes, "total_bytes": total_bytes, "trees_per_rank": sh.num_trees,
+           "copies": copies}
+    if with_e2e:
+        from qattention_b200 import sharding as shd
+        Qp, Kp, Vp = Qh.pin_memory(), Kh.pin_memory(), Vh.pin_memory()
+        Op = torch.empty(sh.num_tokens, H, D, dtype=torch.float16).pin_memory()
+        Lp = torch.empty(sh.num_tokens, H, dtype=torch.float32).pin_memory()
+        e2e_steps = max(3, min(steps, 20))
+
+        def e2e_step():
+            Qd, Kd, Vd = (x.to(dev, non_blocking=True) for x in (Qp, Kp, Vp))
+            Od, Ld = shd.sharded_ragged_attention_with_lse(Qd, Kd, Vd, sh, b, d)
+            Op.copy_(Od, non_blocking=True)
+            Lp.copy_(Ld, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        _barrier(ws)
+        cur = torch.cuda.current_stream(dev)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(cur)
+        for _ in range(e2e_steps):
+            e2e_step()
+        f1.record(cur)
+        torch.cuda.synchronize(dev)
+        e2e_ms = _max_over_ranks(f0.elapsed_time(f1) / e2e_steps, ws)
+        res["e2e"] = {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                      "h2d_bytes_per_step": 3 * B * N * H * D * 2, "d2h_bytes_per_step": B * N * H * (2 * D + 4),
+                      "what": "each rank: H2D of its trees' Q/K/V from pinned memory, "
+                              "sharding.sharded_ragged_attention_with_lse, D2H of O and LSE; bytes summed over ranks"}
+    if with_gather:
+        _barrier(ws)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        Og, Lg = sharding.gather_outputs(O, L, sh, dst=0)
+        torch.cuda.synchronize(dev)
+        g_ms = _max_over_ranks((time.perf_counter() - t0) * 1e3, ws)
+        res["gather"] = {"ms": g_ms, "bytes": B * N * H * (2 * D + 4),
+                         "what": "one torch.distributed.gather of O and one of LSE to rank 0 (NCCL), "
+                                 "wall clock max over ranks, after the timed region"}
+        if rank == 0:
+            eo, el = _oracle_check(Og.cpu(), Lg.cpu(), cfg, sorted({0, B - 1}))
+            res["check"] = {"trees": sorted({0, B - 1}), "heads": 8, "max_abs_err_o": eo,
+                            "max_abs_err_lse": el, "tolerance": "1e-2 (O), 1e-3 (LSE)",
+                            "ok": bool(eo <= 1e-2 and el <= 1e-3)}
+            res["checksum"] = [float(Og.float().sum()), float(Lg.double().sum())]
+    return res, (O, L)
+
+
+def run_ours(args):
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    cfg = args.config
+    B, b, d, H, D = CONFIGS[cfg]
+    N = _num_nodes(b, d)
+    clocks = ClockSampler(local)
+    if rank == 0:
+        clocks.start()
+    head, (O, L) = ancestor_sharded(cfg, ws, rank, dev, args.steps, args.warmup, clocks)
+    if rank == 0:
+        clocks.stop()
+    peak, peak_kind = _peaks()
+    traffic = _traffic_from_profile(cfg)
+    if traffic is not None:  # the profile holds one full-batch launch; this rank's launch covers its share
+        traffic = traffic * head["local_bytes"] / head["total_bytes"]
+
+    secondary = {}
+    if args.secondary:
+        other = "C2" if cfg == "C3" else "C3"
+        sec, ours_other = ancestor_sharded(other, ws, rank, dev, args.steps, args.warmup, None,
+                                           with_e2e=False, with_gather=True)
+        secondary[other] = sec
+        if ws == 1:
+            secondary["triton_reference"] = {
+                cfg: time_triton_reference(cfg, dev, args.steps, args.warmup, (O, L)),
+                other: time_triton_reference(other, dev, args.steps, args.warmup, ours_other)}
+            torch.cuda.empty_cache()
+            secondary["C4_prefix"] = measure_prefix(dev, max(args.steps, 10), args.warmup)
+            secondary["C4_verify_attention"] = measure_hybrid(dev, max(args.steps, 10), args.warmup)
+            torch.cuda.empty_cache()
+            secondary["w4a16_layer"] = measure_w4a16(dev, max(args.steps, 20), args.warmup,
+                                                     [int(m) for m in args.w4_m.split(",")])
+            torch.cuda.empty_cache()
+        secondary["C5_verify_step"] = measure_verify(ws, rank, dev, args.steps, args.warmup, args.verify_layers)
+
+    if rank != 0:
+        return
+    cpu_base = None
+    if ws == 1 and not args.skip_cpu:
+        torch.set_num_threads(os.cpu_count() or 1)
+        Qh, Kh, Vh, _ = make_trees(cfg, 0, 1, 0)
+        heads = cpu_sample_plan(Qh, Kh, Vh, cfg, 2.0)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            cpu_reference_step(Qh, Kh, Vh, cfg, heads)
+            n += 1
+            if time.perf_counter() - t0 > args.cpu_seconds:
+                break
+        cdt = (time.perf_counter() - t0) / n
+        cpu_base = {"value": algorithmic_bytes(N, heads, D) / cdt / 1e9, "unit": "GB/s",
+                    "cores": torch.get_num_threads(), "kind": "port",
+                    "sample": f"{n} runs x 1 of {B} trees x {heads} of {H} heads (padded masked SDPA, fp32, "
+                              "torch CPU); GB/s from that sample's own algorithmic bytes"}
+    ms = head["ms_per_step"]
+    line = {
+        "metric": METRIC, "value": head["gbs"], "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "us_per_step": ms * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": {**_config_dict(cfg, ws),
+                                        "graphs": "8 back-to-back steps per CUDA graph over the rotating copies "
+                                                  "(programmatic dependent launch between steps)"},
+        "roofline": {"bound": "hbm", "achieved": head["per_gpu_gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": head["per_gpu_gbs"] / peak, "peak_kind": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes": head["local_bytes"],
+                     "per": "rank 0's launch (its share of the batch)",
+                     "kernel": "ancestor_tc_kernel (qa_ancestor_attn)"},
+        "cpu_baseline": cpu_base,
+        "e2e": head["e2e"],
+        "gather": head.get("gather"), "check": head.get("check"),
+        "gpu_launches": args.steps, "gpu_launches_per": "rank (one ancestor_tc_kernel per step)",
+        "clocks": clocks.summary(),
+        "checksum": head.get("checksum"),
+        "secondary": secondary,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_kernel_arm(args):
+    """Stand-alone secondary arms, one JSON line each."""
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    clocks = ClockSampler(local)
+    if rank == 0:
+        clocks.start()
+    clocks.mark("t0")
+    if args.kernel == "prefix":
+        r = measure_prefix(dev, args.steps, args.warmup)
+        line = {"metric": "prefix pass TFLOP/s", "value": r["tflops"], "unit": "TFLOP/s", "higher_is_better": True,
+                "ms_per_step": r["us"] * 1e-3, "roofline": {"bound": "tensor", "achieved": r["tflops"],
+                                                            "peak": r["peak"], "unit": "TFLOP/s", "frac": r["frac"],
+                                                            "peak_kind": r["peak_kind"]}, "detail": r}
+    elif args.kernel == "hybrid":
+        r = measure_hybrid(dev, args.steps, args.warmup)
+        line = {"metric": "tree-verify attention us (prefix + tree, merged)", "value": r["us"], "unit": "us",
+                "higher_is_better": False, "ms_per_step": r["us"] * 1e-3, "detail": r}
+    elif args.kernel == "w4a16":
+        r = measure_w4a16(dev, args.steps, args.warmup, [int(m) for m in args.w4_m.split(",")])
+        m = "64" if "64" in r["sweep"] else min(r["sweep"], key=int)
+        v = r["sweep"][m]
+        line = {"metric": f"W4A16 weight-stream GB/s (M={m})", "value": v["weight_gbs"], "unit": "GB/s",
+                "higher_is_better": True, "ms_per_step": v["us_per_layer"] * 1e-3,
+                "roofline": {"bound": "hbm", "achieved": v["weight_gbs"], "peak": r["hbm_peak"], "unit": "GB/s",
+                             "frac": v["hbm_frac"], "peak_kind": r["hbm_peak_kind"]}, "detail": r}
+    elif args.kernel == "verify":
+        r = measure_verify(ws, rank, dev, args.steps, args.warmup, args.verify_layers)
+        line = {"metric": "W4A16 verify-step tokens/s", "value": r.get("tokens_per_s"), "unit": "tokens/s",
+                "higher_is_better": True, "scaling": "strong", "ms_per_step": r.get("ms_per_step"), "detail": r}
+    else:  # "triton": the reference's Triton kernel alone on the selected config
+        r = time_triton_reference(args.config, dev, args.steps, args.warmup)
+        line = {"metric": "reference Triton ancestor kernel GB/s", "value": r.get("gbs"), "unit": "GB/s",
+                "higher_is_better": True, "detail": r}
+    clocks.mark("t1")
+    if rank == 0:
+        clocks.stop()
+        line.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "dtype": "f16",
+                     "data": "synthetic", "clocks": clocks.summary()})
+        print(json.dumps(line), flush=True)
 
 
 def _finish():
@@ -640,28 +848,25 @@ def _finish():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default=HEADLINE, choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--kernel", default="ancestor", choices=["ancestor", "prefix", "hybrid", "w4a16", "verify"])
+    ap.add_argument("--no-secondary", dest="secondary", action="store_false",
+                    help="headline only (no C2/C4/C5/W4A16/Triton measurements)")
+    ap.add_argument("--kernel", default="ancestor",
+                    choices=["ancestor", "prefix", "hybrid", "w4a16", "verify", "triton"])
     ap.add_argument("--verify-layers", type=int, default=0, help="override the layer count (tests only)")
-    ap.add_argument("--w4-m", default="16,64,1023,8184", help="token counts of the w4a16 arm")
+    ap.add_argument("--w4-m", default="16,64,1023,8184", help="token counts of the w4a16 measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.kernel == "prefix":
-        run_prefix(args)
-    elif args.kernel == "hybrid":
-        run_hybrid(args)
-    elif args.kernel == "w4a16":
-        run_w4a16(args)
-    elif args.kernel == "verify":
-        run_verify(args)
+    elif args.kernel != "ancestor":
+        run_kernel_arm(args)
     else:
         run_ours(args)
     _finish()

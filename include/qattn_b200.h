@@ -196,8 +196,12 @@ QA_API int qa_w4a16_gemm(const qa_w4a16_args* args, void* stream);
  * owns, or a serving loop where an allocation's implicit device synchronisation
  * would stall other streams). No counterpart in the reference.
  * The split-K partial sums go to a fixed 16 MiB array inside the library
- * (4 Mi floats: splits * M * N must not exceed it, else QA_ERR_INVALID); every
- * GPU that loads the library holds that array until the process exits.
+ * (4 Mi floats); every GPU that loads the library holds that array until the
+ * process exits. The split count is first clamped as in qa_w4a16_gemm (at most
+ * K/128, no empty split). With splits = 0 (automatic) a count whose partials
+ * (splits * M * N floats) would not fit steps down to the largest that does,
+ * down to 1, which needs no scratch; an explicit split count that does not fit
+ * returns QA_ERR_INVALID.
  * `workspace` in args is ignored. The first call on each device looks up the
  * array's device address (make that first call before any stream capture).
  * All calls share the array: calls that overlap on the GPU (other streams,

@@ -298,11 +298,9 @@ cudaError_t launch_d(AncParams& p, bool parents, cudaStream_t st) {
   p.rows_cap = cap < cap_max ? cap : cap_max;
   const int smem = TL::MQ * D * int(sizeof(T)) + p.rows_cap * row_bytes;
   auto kern = parents ? ancestor_attn_kernel<T, D, true> : ancestor_attn_kernel<T, D, false>;
-  static bool attr_set[2] = {false, false};  // per instance, once per process
-  if (!attr_set[parents]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  {
+    const cudaError_t e = qa_smem_attr(reinterpret_cast<const void*>(kern), kMaxSmem);
     if (e != cudaSuccess) return e;
-    attr_set[parents] = true;
   }
   kern<<<dim3{unsigned(blocks)}, kThreads, smem, st>>>(p);
   return cudaGetLastError();

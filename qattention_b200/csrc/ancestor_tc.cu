@@ -618,20 +618,25 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
 // (memoised: the size depends only on the tree shape).
 template <typename T, int D, int NBK, int MINB, bool SUB>
 int resident_ctas(int smem) {
-  // (smem << 32 | occupancy) of the last query; atomic so that host threads
-  // launching concurrently read a consistent pair
-  static std::atomic<int64_t> memo{-1};
-  const int64_t m = memo.load(std::memory_order_relaxed);
+  // (smem << 32 | occupancy) of the last query on each device; atomic so that
+  // host threads launching concurrently read a consistent pair
+  static std::atomic<int64_t> memo[kQaMaxDevices];
+  static std::once_flag init;
+  std::call_once(init, [] {
+    for (auto& x : memo) x.store(-1);
+  });
+  const int dev = qa_current_device();
+  const int64_t m = memo[dev].load(std::memory_order_relaxed);
   if (m >= 0 && int(m >> 32) == smem) return int(m & 0xffffffff);
   {
-    if (cudaFuncSetAttribute(ancestor_tc_kernel<T, D, NBK, MINB, SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kTcMaxSmem) != cudaSuccess)
+    if (qa_smem_attr(reinterpret_cast<const void*>(ancestor_tc_kernel<T, D, NBK, MINB, SUB>), kTcMaxSmem) !=
+        cudaSuccess)
       return 0;
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ancestor_tc_kernel<T, D, NBK, MINB, SUB>, kTcThreads,
                                                       smem) != cudaSuccess)
       return 0;
-    memo.store((int64_t(smem) << 32) | int64_t(occ), std::memory_order_relaxed);
+    memo[dev].store((int64_t(smem) << 32) | int64_t(occ), std::memory_order_relaxed);
     return occ;
   }
 }
@@ -785,12 +790,7 @@ int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
   p.head_ratio = a.num_q_heads / a.num_kv_heads;
   p.rows_cap = rows;
   p.kw_cap = plan.kw_cap;
-  {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&p.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return QA_ERR_LAUNCH;
-  }
+  p.num_sms = qa_sm_count();
   p.div_b = make_fast_div(uint32_t(a.branching));
   const bool bf = a.dtype == QA_DTYPE_BF16;
   switch (a.head_dim) {

@@ -447,13 +447,8 @@ int launch(const qa_prefix_args& a, cudaStream_t st) {
   p.scale_log2 = a.scale * kLog2e;
   const int64_t blocks = int64_t(a.batch) * a.num_kv_heads * p.m_tiles;
   if (blocks > 0x7fffffffLL) return QA_ERR_INVALID;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(prefix_attn_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             PfxSmem<D>::TOTAL) != cudaSuccess)
-      return QA_ERR_LAUNCH;
-    attr_set = true;
-  }
+  if (qa_smem_attr(reinterpret_cast<const void*>(prefix_attn_kernel<T, D>), PfxSmem<D>::TOTAL) != cudaSuccess)
+    return QA_ERR_LAUNCH;
   prefix_attn_kernel<T, D><<<dim3{unsigned(blocks)}, kThreads, PfxSmem<D>::TOTAL, st>>>(qm, km, vm, p);
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }

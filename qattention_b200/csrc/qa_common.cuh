@@ -12,6 +12,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+#include <vector>
+
 #include "../../include/qattn_b200.h"
 
 #define QA_DEVINL __device__ __forceinline__
@@ -137,6 +141,54 @@ QA_DEVINL float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// ---- host-side per-device launch state --------------------------------------
+// Kernel attributes (the dynamic shared-memory limit) and device properties are
+// per device: a process that launches on several GPUs must set and query them
+// on each. These helpers key everything by the current device and are safe to
+// call from several host threads at once.
+constexpr int kQaMaxDevices = 64;
+
+inline int qa_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kQaMaxDevices) dev = 0;
+  return dev;
+}
+
+// Raises `fn`'s dynamic shared-memory limit to at least `bytes` on the current
+// device (once per device, kernel and size).
+inline cudaError_t qa_smem_attr(const void* fn, int bytes) {
+  struct Entry {
+    int dev;
+    const void* fn;
+    int bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> done;
+  const int dev = qa_current_device();
+  std::lock_guard<std::mutex> lock(mu);
+  for (Entry& e : done)
+    if (e.dev == dev && e.fn == fn) {
+      if (e.bytes >= bytes) return cudaSuccess;
+      const cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (r == cudaSuccess) e.bytes = bytes;
+      return r;
+    }
+  const cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (r == cudaSuccess) done.push_back({dev, fn, bytes});
+  return r;
+}
+
+// Streaming multiprocessors of the current device (cached per device).
+inline int qa_sm_count() {
+  static std::atomic<int> cache[kQaMaxDevices];
+  const int dev = qa_current_device();
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  cache[dev].store(n, std::memory_order_relaxed);
+  return n;
 }
 
 }  // namespace qa

@@ -434,15 +434,7 @@ bool make_x_map(CUtensorMap* map, const void* x, int K, int M, int64_t x_stride,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  }
-  return n;
-}
+int sm_count() { return qa_sm_count(); }
 
 }  // namespace
 
@@ -523,13 +515,7 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   auto kern = sh.cps == 2 ? (split ? w4a16_gemm_kernel<1, true, 2> : w4a16_gemm_kernel<1, false, 2>)
             : sh.ft == 2  ? (split ? w4a16_gemm_kernel<2, true, 1> : w4a16_gemm_kernel<2, false, 1>)
                           : (split ? w4a16_gemm_kernel<1, true, 1> : w4a16_gemm_kernel<1, false, 1>);
-  static bool attr[6] = {false, false, false, false, false, false};
-  const int ai = (sh.cps == 2 ? 4 : (sh.ft - 1) * 2) + split;
-  if (!attr[ai]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return QA_ERR_LAUNCH;
-    attr[ai] = true;
-  }
+  if (qa_smem_attr(reinterpret_cast<const void*>(kern), smem) != cudaSuccess) return QA_ERR_LAUNCH;
   const int threads = 96 + sh.ft * 256;
   // both kernels are launched as programmatic dependents of their predecessor
   cudaLaunchAttribute pdl[1];
@@ -660,10 +646,22 @@ extern "C" int qa_w4a16_gemm_noalloc(const qa_w4a16_args* args, void* stream) {
   qa_w4a16_args a = *args;
   if (a.M < 0 || a.N <= 0 || a.K <= 0 || a.K % 128 != 0 || a.N % 128 != 0 || a.splits < 0) return QA_ERR_INVALID;
   if (a.M == 0) return QA_OK;
-  // The split count the GEMM will use is at most this (it only ever lowers it).
-  const int splits = a.splits == 0 ? w4a16_auto_splits(a.M, a.N, a.K) : a.splits;
+  // The split count after the same clamps qa_w4a16_gemm applies (at most one
+  // split per K step, no empty split), so the size check sees the count that runs.
+  const int k_tiles = a.K / kBK;
+  auto effective = [k_tiles](int s) {
+    s = s < 1 ? 1 : (s > k_tiles ? k_tiles : s);
+    const int per = (k_tiles + s - 1) / s;
+    return (k_tiles + per - 1) / per;
+  };
+  const int64_t mn = int64_t(a.M) * a.N;
+  int splits = effective(a.splits == 0 ? w4a16_auto_splits(a.M, a.N, a.K) : a.splits);
+  if (splits > 1 && int64_t(splits) * mn > kNoAllocScratchFloats) {
+    if (a.splits != 0) return QA_ERR_INVALID;  // an explicit split count beyond the fixed scratch
+    // automatic mode: the largest split count whose partials fit (1 needs none)
+    while (splits > 1 && int64_t(splits) * mn > kNoAllocScratchFloats) splits = effective(splits - 1);
+  }
   if (splits > 1) {
-    if (int64_t(splits) * a.M * a.N > kNoAllocScratchFloats) return QA_ERR_INVALID;  // beyond the fixed scratch
     float* scratch = nullptr;
     const int st = scratch_for_current_device(&scratch);
     if (st != QA_OK) return st;

@@ -38,7 +38,7 @@ def _pair(M, N, K, splits, seed):
     L = _lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
     y_ref = torch.empty(M, N, dtype=torch.float16, device="cuda")
-    ws = torch.empty(max(splits, 1) * M * N, dtype=torch.float32, device="cuda")
+    ws = torch.empty(max(splits, 32) * M * N, dtype=torch.float32, device="cuda")
     assert L.qa_w4a16_gemm(_args(x, qw, sc, y_ref, ws, M, N, K, splits), stream) == 0
     y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
     assert L.qa_w4a16_gemm_noalloc(_args(x, qw, sc, y, None, M, N, K, splits), stream) == 0
@@ -70,3 +70,15 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     rc = _lib.lib().qa_w4a16_gemm_noalloc(_args(x, qw, sc, y, None, 64, 14336, 4096, 8),
                                           torch.cuda.current_stream().cuda_stream)
     assert rc == -1
+
+
+@pytest.mark.parametrize("M,N,K,splits", [
+    (24, 512, 1024, 0),     # automatic split count, small shape
+    (64, 14336, 4096, 0),   # automatic: 8 splits would not fit the array, so it steps down
+    (16, 256, 512, 9),      # more splits than K steps (4): clamped before the size check
+    (32, 1024, 2048, 1),    # one split: no scratch at all
+])
+def test_noalloc_split_resolution(M, N, K, splits):
+    y, y_ref = _pair(M, N, K, splits, 11)
+    _close(y, y_ref)
+    assert _lib.device_error() == 0
