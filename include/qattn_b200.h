@@ -69,8 +69,12 @@ extern "C" {
  * page_table != NULL, K and V are caches [pages, page_size, kv_heads, D] and the KV row of
  * sequence b's node n (plus kv_offset) is slot (n % page_size) of physical page
  * page_table[b * page_table_stride + n / page_size]; k/v_stride_t are then the slot
- * strides and k/v_stride_page the page strides (elements). Complete-tree mode only
- * (parents == NULL, branching >= 2, head_dim 64/128/256); otherwise QA_ERR_UNSUPPORTED. */
+ * strides and k/v_stride_page the page strides (elements). Every mode takes a page
+ * table: complete trees (tensor-core tiles), chains (branching 1) and explicit parents
+ * (the per-query walk).
+ * Batched queries: q_stride_b = 0 reads query rows packed at cu_seqlens_q; a nonzero
+ * q_stride_b places the query row of sequence b's node n at b*q_stride_b + n*q_stride_t
+ * (a [B, N, H, D] view of any batch pitch, read in place; o and lse stay packed). */
 typedef struct qa_ancestor_args {
   const void* q;
   const void* k;
@@ -103,6 +107,7 @@ typedef struct qa_ancestor_args {
   int64_t page_table_stride;    /* elements between sequences' rows of page_table */
   int64_t k_stride_page, v_stride_page;  /* paged K/V: elements between pages */
   int32_t page_size;            /* paged K/V: tokens per page */
+  int64_t q_stride_b;           /* 0: packed query rows; else batch stride (see above) */
 } qa_ancestor_args;
 
 QA_API int qa_ancestor_attn(const qa_ancestor_args* args, void* stream);

@@ -55,6 +55,7 @@ class AncestorArgs(Structure):
         ("scale", c_float), ("dtype", c_int32),
         ("page_table", c_void_p), ("page_table_stride", c_int64),
         ("k_stride_page", c_int64), ("v_stride_page", c_int64), ("page_size", c_int32),
+        ("q_stride_b", c_int64),
     ]
 
 

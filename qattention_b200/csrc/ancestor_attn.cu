@@ -144,6 +144,23 @@ QA_DEVINL float reduce_lanes(float s, unsigned mask) {
   return s;
 }
 
+// Element offsets of the K and V rows of sequence `seq`'s node `node`: packed
+// K/V at token kv0 + node, or (paged) slot (kv_offset + node) % page_size of the
+// physical page the sequence's page-table row names for it.
+QA_DEVINL void kv_offsets(const qa_ancestor_args& a, int seq, int kv0, int node, int64_t& ko, int64_t& vo) {
+  if (a.page_table == nullptr) {
+    const int64_t tk = int64_t(kv0) + node;
+    ko = tk * a.k_stride_t;
+    vo = tk * a.v_stride_t;
+  } else {
+    const int pos = a.kv_offset + node;
+    const int64_t page = __ldg(a.page_table + int64_t(seq) * a.page_table_stride + pos / a.page_size);
+    const int slot = pos % a.page_size;
+    ko = page * a.k_stride_page + int64_t(slot) * a.k_stride_t;
+    vo = page * a.v_stride_page + int64_t(slot) * a.v_stride_t;
+  }
+}
+
 template <typename T, int D, bool PARENTS>
 __global__ void __launch_bounds__(kThreads) ancestor_attn_kernel(const AncParams p) {
   using TL = Tile<D>;
@@ -185,7 +202,7 @@ __global__ void __launch_bounds__(kThreads) ancestor_attn_kernel(const AncParams
   // ---- stage the tile's Q rows ----
   for (int c = tid; c < nq * RC; c += kThreads) {
     const int r = c / RC, cc = c - r * RC;
-    cp_async16(sQ + r * D + cc * 8, Qh + (int64_t(q0) + q_lo + r) * a.q_stride_t + cc * 8);
+    cp_async16(sQ + r * D + cc * 8, Qh + q_seq_off(a, seq, q0) + int64_t(q_lo + r) * a.q_stride_t + cc * 8);
   }
   __syncthreads();
   // ---- stage every window's K and V rows ----
@@ -194,9 +211,10 @@ __global__ void __launch_bounds__(kThreads) ancestor_attn_kernel(const AncParams
     const int j = c / RC, cc = c - j * RC;
     int w = 0;
     while (w + 1 < nw && win_base[w + 1] <= j) ++w;
-    const int64_t tk = int64_t(kv0) + win_lo[w] + (j - win_base[w]);
-    cp_async16(sK + j * D + cc * 8, Kh + tk * a.k_stride_t + cc * 8);
-    cp_async16(sV + j * D + cc * 8, Vh + tk * a.v_stride_t + cc * 8);
+    int64_t ko, vo;
+    kv_offsets(a, seq, kv0, win_lo[w] + (j - win_base[w]), ko, vo);
+    cp_async16(sK + j * D + cc * 8, Kh + ko + cc * 8);
+    cp_async16(sV + j * D + cc * 8, Vh + vo + cc * 8);
   }
   cp_async_wait_all();
   __syncthreads();
@@ -259,10 +277,11 @@ __global__ void __launch_bounds__(kThreads) ancestor_attn_kernel(const AncParams
       ++s;
     }
     while (node >= 0) {  // explicit parents / levels past the staged ones
-      const int64_t tk = int64_t(kv0) + node;
+      int64_t ko, vo;
+      kv_offsets(a, seq, kv0, node, ko, vo);
       uint4 ka, kb, va, vb;
-      ldg_row<T, D>(Kh + tk * a.k_stride_t, li, ka, kb);
-      ldg_row<T, D>(Vh + tk * a.v_stride_t, li, va, vb);
+      ldg_row<T, D>(Kh + ko, li, ka, kb);
+      ldg_row<T, D>(Vh + vo, li, va, vb);
       const float sc = reduce_lanes<LPI>(dot16<T>(qa, qb, ka, kb), mask) * p.scale_log2;
       softmax_step<T, LPI>(st, sc, va, vb);
       node = advance(node, s);
@@ -340,7 +359,7 @@ extern "C" int qa_ancestor_attn(const qa_ancestor_args* args, void* stream) {
   if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || !aligned16(a.o) ||
       (a.prefix_o && !aligned16(a.prefix_o)))
     return QA_ERR_ALIGN;
-  if (!stride_ok(a.q_stride_t) || !stride_ok(a.q_stride_h) || !stride_ok(a.k_stride_t) ||
+  if (!stride_ok(a.q_stride_t) || !stride_ok(a.q_stride_h) || !stride_ok(a.q_stride_b) || !stride_ok(a.k_stride_t) ||
       !stride_ok(a.k_stride_h) || !stride_ok(a.v_stride_t) || !stride_ok(a.v_stride_h) ||
       !stride_ok(a.o_stride_t) || !stride_ok(a.o_stride_h))
     return QA_ERR_ALIGN;
@@ -355,13 +374,12 @@ extern "C" int qa_ancestor_attn(const qa_ancestor_args* args, void* stream) {
   p.tiles_per_seq = (a.max_seqlen + mq - 1) / mq;
   const bool parents = a.parents != nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (a.page_table != nullptr) {  // paged K/V: the tensor-core kernel only
-    if (a.page_size <= 0 || a.page_table_stride < 0 || a.parents != nullptr) return QA_ERR_INVALID;
+  if (a.page_table != nullptr) {  // paged K/V: both kernels look the rows up in the page table
+    if (a.page_size <= 0 || a.page_table_stride < 0) return QA_ERR_INVALID;
     if (!stride_ok(a.k_stride_page) || !stride_ok(a.v_stride_page)) return QA_ERR_ALIGN;
   }
   const int tc = ancestor_tc_launch(a, st);
   if (tc != kTcNotApplicable) return tc;
-  if (a.page_table != nullptr) return QA_ERR_UNSUPPORTED;
   p.div_b = make_fast_div(uint32_t(parents ? 1 : a.branching));
   cudaError_t e = (a.dtype == QA_DTYPE_F16) ? launch_t<__half>(p, parents, st)
                                             : launch_t<__nv_bfloat16>(p, parents, st);

@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   auto issue_qk = [&](int hh) {
     if constexpr (SUB) {
       const char* Qh = reinterpret_cast<const char*>(a.q) +
-                       int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + int64_t(q0) * a.q_stride_t + my_cc * 8);
+                       int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + q_seq_off(a, seq, q0) + my_cc * 8);
       const int64_t tstep = a.q_stride_t * int64_t(sizeof(T));
       uint32_t d = sQa + uint32_t(my_r0 * D * 2), x = my_x;
 #pragma unroll
@@ -383,7 +383,8 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       }
     } else {
       const char* src = reinterpret_cast<const char*>(a.q) +
-                        int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + (int64_t(q0) + q_lo + my_r0) * a.q_stride_t + my_cc * 8);
+                        int64_t(sizeof(T)) * (int64_t(hh) * a.q_stride_h + q_seq_off(a, seq, q0) +
+                                              int64_t(q_lo + my_r0) * a.q_stride_t + my_cc * 8);
       const int64_t step = int64_t(RPP) * a.q_stride_t * int64_t(sizeof(T));
       uint32_t d = sQa + uint32_t(my_r0 * D * 2), x = my_x;
       for (int r = my_r0; r < nq; r += RPP, src += step, d += kRowStep, x ^= kXStep) cp_async16_s(d + x, src);

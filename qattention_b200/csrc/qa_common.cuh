@@ -137,6 +137,13 @@ struct FastDiv {
 };
 QA_DEVINL uint32_t fast_div(uint32_t x, FastDiv f) { return (__umulhi(x, f.m) + x) >> f.l; }
 
+// Element offset of sequence `seq`'s first query row: its own batch stride when
+// the caller gave one (queries in a [B, N, ...] view whose batch pitch is not
+// N token rows), else row cu_seqlens_q[seq] = q0 of the packed token axis.
+QA_DEVINL int64_t q_seq_off(const qa_ancestor_args& a, int seq, int q0) {
+  return a.q_stride_b != 0 ? int64_t(seq) * a.q_stride_b : int64_t(q0) * a.q_stride_t;
+}
+
 QA_DEVINL float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -100,8 +100,12 @@ def pack_inputs(
 
 def _ancestor(Q, K, V, cu_dev, max_seqlen, *, branching=1, max_depth=0, parents=None,
               want_lse=False, cu_kv=None, kv_offset=0, prefix_o=None, prefix_lse=None,
-              out=None, lse_out=None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-    """Launch ``qa_ancestor_attn`` on torch's current stream; returns (O, LSE or None)."""
+              out=None, lse_out=None, q_batched=None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Launch ``qa_ancestor_attn`` on torch's current stream; returns (O, LSE or None).
+
+    ``q_batched``: the queries as a ``[B, N, Hq, D]`` view read in place through its
+    batch stride (``Q`` then only gives the packed shape ``[B*N, Hq, D]``).
+    """
     total, Hq, D = Q.shape
     Hkv = K.shape[1]
     if K.shape[2] != D or V.shape[1:] != K.shape[1:]:
@@ -125,6 +129,9 @@ def _ancestor(Q, K, V, cu_dev, max_seqlen, *, branching=1, max_depth=0, parents=
     a.cu_seqlens_kv = cu_kv.data_ptr() if cu_kv is not None else None
     a.parents = parents.data_ptr() if parents is not None else None
     a.q_stride_t, a.q_stride_h = Q.stride(0), Q.stride(1)
+    if q_batched is not None:
+        a.q = q_batched.data_ptr()
+        a.q_stride_b, a.q_stride_t, a.q_stride_h = q_batched.stride(0), q_batched.stride(1), q_batched.stride(2)
     a.k_stride_t, a.k_stride_h = K.stride(0), K.stride(1)
     a.v_stride_t, a.v_stride_h = V.stride(0), V.stride(1)
     a.o_stride_t, a.o_stride_h = O.stride(0), O.stride(1)
@@ -221,8 +228,9 @@ def ragged_attention_paged(
     of sequence b's logical page p; token n of sequence b (its BFS node n) is slot
     ``n % page_size`` of page ``page_table[b, n // page_size]``. Returns O like ``Q``.
     Mirrors src/ragged_attn.py:934-1004; the walk, the duplicate rule and the result
-    are those of :func:`ragged_attention`. The page lookup happens once per staged row
-    of a tile (not per walk step), in the tensor-core kernel.
+    are those of :func:`ragged_attention`. Complete trees (b >= 2) look a page up once
+    per staged row of a tile in the tensor-core kernel; chains (b = 1) take the per-query
+    walk, which looks up each row it stages or reads.
     """
     assert K_cache.shape == V_cache.shape, "K and V cache shapes must match"
     assert Q.dtype in _SUPPORTED and Q.dtype == K_cache.dtype == V_cache.dtype, (
@@ -237,8 +245,8 @@ def ragged_attention_paged(
     _, page_size, Hkv, Dk = K_cache.shape
     if Dk != D or Hq % Hkv != 0:
         raise ValueError(f"cache [.., {Hkv}, {Dk}] does not match Q [.., {Hq}, {D}]")
-    if branching_factor < 2:
-        raise ValueError("the paged walk needs branching_factor >= 2 (complete trees)")
+    if branching_factor < 1:
+        raise ValueError(f"branching_factor must be >= 1, got {branching_factor}")
     if max_depth < 0:
         raise ValueError(f"max_depth must be >= 0, got {max_depth}")
     cu_dev, ms = _cu_and_max(cu_seqlens, None, Q.device)
@@ -450,8 +458,16 @@ def tree_verify_attention(
     par = None
     if tree_parents is not None:
         par = tree_parents.to(device=Q.device, dtype=torch.int32).repeat(B).contiguous()
-    # Query rows need one token stride across the batch: copy Q once unless it already has it.
-    Qr = (Qt if Qt.is_contiguous() else Qt.contiguous()).view(B * N, Hq, D)
+    # Queries are read in place: as packed rows when the batch pitch is N token rows (a
+    # head slice of a fused qkv projection), else through the kernel's batch stride
+    # (e.g. a contiguous [B, Hq, N, D] tensor); only a misaligned view is copied.
+    q_batched = None
+    if Qt.stride(3) != 1 or any(x % 8 for x in Qt.stride()[:3]) or Qt.data_ptr() % 16:
+        Qr = Qt.contiguous().view(B * N, Hq, D)
+    elif Qt.stride(0) == N * Qt.stride(1):
+        Qr = Qt.as_strided((B * N, Hq, D), (Qt.stride(1), Qt.stride(2), 1), Qt.storage_offset())
+    else:
+        Qr, q_batched = out.view(B * N, Hq, D), Qt  # Qr only carries the packed shape
     Kr, Vr, kv_rows, kv_off = _tree_rows(Kt, Vt, L, N)
     cu_q = torch.arange(0, (B + 1) * N, N, dtype=torch.int32, device=Q.device)
     cu_kv = torch.arange(0, (B + 1) * kv_rows, kv_rows, dtype=torch.int32, device=Q.device)
@@ -459,7 +475,7 @@ def tree_verify_attention(
               cu_kv=cu_kv, kv_offset=kv_off,
               prefix_o=out.view(B * N, Hq, D) if L > 0 else None,
               prefix_lse=lse.view(B * N, Hq) if L > 0 else None,
-              out=out.view(B * N, Hq, D))
+              out=out.view(B * N, Hq, D), q_batched=q_batched)
     return out.permute(0, 2, 1, 3)
 
 

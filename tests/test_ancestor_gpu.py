@@ -230,14 +230,15 @@ def test_batch_permutation_is_bit_exact():
         assert torch.equal(O2[j * N:(j + 1) * N], O[i * N:(i + 1) * N])
 
 
-@pytest.mark.parametrize("cfg", ["C2", "C3"])
-def test_full_size_sliced_against_oracle(cfg):
-    # bench configs C2 and C3 at full size; the oracle checks the first and last tree
+@pytest.mark.parametrize("cfg,dtype", [("C2", torch.float16), ("C3", torch.float16),
+                                       ("C2", torch.bfloat16), ("C3", torch.bfloat16)])
+def test_full_size_sliced_against_oracle(cfg, dtype):
+    # bench configs C2 and C3 at full size, fp16 and bf16; the oracle checks the first and last tree
     B, b, d = (8, 4, 5) if cfg == "C2" else (16, 2, 9)
     H, D = 32, 128
     N = tm.num_tree_nodes(b, d)
     g = torch.Generator().manual_seed(2)
-    Q, K, V = (torch.randn(B * N, H, D, generator=g).half() for _ in range(3))
+    Q, K, V = (torch.randn(B * N, H, D, generator=g).to(dtype) for _ in range(3))
     cu = torch.arange(0, (B + 1) * N, N, dtype=torch.int32)
     O, L = ra.ragged_attention_with_lse(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
     O, L = O.cpu(), L.cpu()
@@ -245,6 +246,7 @@ def test_full_size_sliced_against_oracle(cfg):
     for s in (0, B - 1):
         sl = slice(s * N, (s + 1) * N)
         ro, rl = orc.sparse_ancestor_attention(Q[sl], K[sl], V[sl], [0, N], b, d, dtype=torch.float32)
+        assert O.dtype == dtype
         assert torch.allclose(O[sl].float(), ro, atol=ATOL, rtol=RTOL)
         assert torch.allclose(L[sl], rl, atol=1e-3)
 
@@ -294,6 +296,8 @@ def test_deep_trees_ragged_subtree_tiles(lens, d, H):
     ([15, 9, 40, 15], 2, 3, 4, 4, 64, 16),          # contiguous tiles, ragged, truncated walks
     ([1365, 1000, 1365], 4, 5, 8, 8, 128, 16),      # C2-shaped trees
     ([511, 300, 130, 511], 2, 8, 8, 2, 64, 32),     # deep trees: subtree tiles, GQA
+    ([6, 4, 6, 1], 1, 5, 4, 4, 64, 4),              # chains (b = 1): the per-query walk
+    ([40, 33, 40], 1, 39, 8, 2, 128, 16),           # long chains, GQA, walks past the staged levels
 ])
 def test_paged_kv_matches_packed_and_oracle(lens, b, d, H, Hkv, D, page):
     # src/ragged_attn.py:827-1047: K/V in pages through a page table; the physical
@@ -326,6 +330,6 @@ def test_paged_kv_rejects_unsupported():
     pt = torch.zeros(1, 1, dtype=torch.int32)
     cu = torch.tensor([0, 15], dtype=torch.int32)
     with pytest.raises(ValueError):
-        ra.ragged_attention_paged(Q, Kc, Kc, pt, cu, 1, 3)       # chains are not paged
+        ra.ragged_attention_paged(Q, Kc, Kc, pt, cu, 0, 3)       # branching factor 0
     with pytest.raises(AssertionError):
         ra.ragged_attention_paged(Q, Kc, Kc[:, :8], pt, cu, 2, 3)

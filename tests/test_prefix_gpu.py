@@ -134,3 +134,38 @@ def test_config4_full_size_first_sequence():
         kk, vv = K[s].permute(1, 0, 2), V[s].permute(1, 0, 2)
         ref = orc.prefix_tree_sdpa(q, kk[:L], vv[:L], kk[L:], vv[L:], mask)
         assert torch.allclose(out[s].permute(1, 0, 2), ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("L", [0, 200])
+@pytest.mark.parametrize("use_parents", [False, True])
+def test_tree_verify_query_layouts_read_in_place(L, use_parents):
+    # The queries are read in place in three layouts: a contiguous [B, Hq, N, D]
+    # tensor (the kernel's batch stride), a head slice of a fused qkv projection
+    # (packed rows, one token stride) and an odd offset that forces the copy.
+    # All three must give bit-identical results.
+    B, b, d, Hq, Hkv, D = 3, 2, 5, 8, 2, 64
+    if use_parents:
+        tree = tm.build_pruned_tree(b, d, rng=np.random.default_rng(5))
+        parents = torch.from_numpy(tm.kernel_parents(tree))
+    else:
+        tree, parents = tm.build_tree(b, d), None
+    N = len(tree)
+    g = torch.Generator().manual_seed(17)
+    K = torch.randn(B, Hkv, L + N, D, generator=g).half().cuda()
+    V = torch.randn(B, Hkv, L + N, D, generator=g).half().cuda()
+    Q = torch.randn(B, Hq, N, D, generator=g).half().cuda()
+    qkv = torch.zeros(B, N, Hq + 2 * Hkv, D, dtype=torch.float16, device="cuda")
+    qkv[:, :, :Hq] = Q.permute(0, 2, 1, 3)
+    q_slice = qkv[:, :, :Hq].permute(0, 2, 1, 3)                  # [B, Hq, N, D] view, token pitch (Hq+2Hkv)D
+    buf = torch.zeros(B * Hq * N * D + 4, dtype=torch.float16, device="cuda")
+    q_odd = buf[4:].view(B, Hq, N, D)                              # 8-byte offset: not 16-byte aligned
+    q_odd.copy_(Q)
+    outs = [ra.tree_verify_attention(q, K, V, b, d, tree_parents=parents) for q in (Q, q_slice, q_odd)]
+    assert _lib.device_error() == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    mask = tm.tree_attention_mask_pruned(tree)
+    for s in (0, B - 1):
+        q = Q[s].permute(1, 0, 2).cpu()
+        kk, vv = K[s].permute(1, 0, 2).cpu(), V[s].permute(1, 0, 2).cpu()
+        ref = orc.prefix_tree_sdpa(q, kk[:L], vv[:L], kk[L:], vv[L:], mask)
+        assert torch.allclose(outs[0][s].permute(1, 0, 2).float().cpu(), ref, atol=ATOL, rtol=RTOL)

@@ -69,3 +69,50 @@ def test_gemm_on_gptq_checkpoint_tensors():
     scale = ref.abs().max().item() + 1e-6
     assert (Y - ref).abs().max().item() <= 2e-3 * scale + 1e-3
     assert torch.equal(qw2, qw) and torch.equal(sc2, sc)
+
+
+# The four W4A16 GEMMs of one Llama-3.1-8B decoder layer as the bench runs them
+# (q/k/v and gate/up fused along N; the linears the reference's E2E script runs
+# through Marlin, scripts/w4a16_e2e.py:698-699), at the token counts of the
+# bench sweep. The automatic split count is what the bench uses (qkv 6, o 8,
+# down 9 and gate_up 1 at small M), and M = 8184 takes the large-M tile shape.
+# The fp64 oracle runs on a fixed sample of 64 rows x every column.
+LLAMA_LAYER = [("qkv", 4096, 6144), ("o", 4096, 4096), ("gate_up", 4096, 28672), ("down", 14336, 4096)]
+_layer_cache = {}
+
+
+def _layer_weights(name, K, N):
+    if name not in _layer_cache:
+        qw, sc = _weights(K, N, 1000 + [n for n, _, _ in LLAMA_LAYER].index(name))
+        q = quant.unpack_int4(qw).numpy().astype(np.uint8)
+        _layer_cache[name] = (qw.cuda(), sc.cuda(), wo.dequantize(q, sc.numpy()))  # W' fp16 [K, N]
+    return _layer_cache[name]
+
+
+def _oracle_rows(Xs, W):
+    """fp64 product of sampled activation rows with the dequantised weights, column chunk by chunk."""
+    out = np.empty((Xs.shape[0], W.shape[1]), dtype=np.float32)
+    X64 = Xs.astype(np.float64)
+    for c in range(0, W.shape[1], 4096):
+        out[:, c:c + 4096] = X64 @ W[:, c:c + 4096].astype(np.float64)
+    return out
+
+
+@pytest.mark.parametrize("name,K,N", LLAMA_LAYER)
+@pytest.mark.parametrize("M", [16, 64, 1023, 8184])
+def test_llama_layer_shapes_vs_oracle(name, K, N, M):
+    import ctypes
+    qw, sc, W = _layer_weights(name, K, N)
+    g = torch.Generator().manual_seed(M + K + N)
+    X = torch.randn(M, K, generator=g).half()
+    Y = quant.w4a16_linear(X.cuda(), qw, sc).float().cpu()
+    assert _lib.device_error() == 0
+    rows = torch.unique(torch.cat([torch.tensor([0, M - 1]),
+                                   torch.randint(0, M, (62,), generator=g)]))[:64] if M > 64 else torch.arange(M)
+    ref = torch.from_numpy(_oracle_rows(X[rows].numpy(), W))
+    scale = ref.abs().max().item() + 1e-6
+    err = (Y[rows] - ref).abs().max().item()
+    sp, wb = ctypes.c_int32(), ctypes.c_int64()
+    _lib.check(_lib.lib().qa_w4a16_plan(M, N, K, ctypes.byref(sp), ctypes.byref(wb)), "qa_w4a16_plan")
+    assert err <= 2e-3 * scale + 1e-3, f"{name} M={M} splits={sp.value}: max err {err:.3e} (max |ref| {scale:.3e})"
+    assert torch.isfinite(Y).all()
