@@ -254,9 +254,21 @@ QA_API int qa_silu_mul(const void* gate_up, void* out, int32_t M, int32_t F, voi
  * Reads and clears the device error flag that the tensor-core kernels set when
  * one of their bounded pipeline waits times out (a kernel that hits it stops,
  * frees its resources and leaves its outputs incomplete). Synchronising call.
- * *flag = 0 means no kernel has reported an error since the last call.
+ * *flag = 0 means no kernel has reported an error since the last call; bit 4
+ * means a plan check of the ancestor kernel failed (see qa_ancestor_diagnostics).
  */
 QA_API int qa_check_device_error(int* flag);
+
+/*
+ * Diagnostics of the tensor-core ancestor kernel (no counterpart in the
+ * reference, whose kernels do not check their index arithmetic): before it
+ * stages a tile, the kernel checks that every query row, staged K/V row and key
+ * slot of the tile's plan lies inside its sequence; a tile that fails is skipped
+ * (its outputs are not written) and the first failure is recorded. out8 (may be
+ * NULL) receives [check 1..4 or 0, tile, sequence, value, plan from table,
+ * sequence length, tile rows, staged rows]; the record is cleared. Synchronising.
+ */
+QA_API int qa_ancestor_diagnostics(int32_t* out8);
 
 /* Human-readable name of a status code (static storage). */
 QA_API const char* qa_status_string(int status);

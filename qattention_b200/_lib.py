@@ -25,6 +25,7 @@ EXPORTED = (
     "qa_lse_merge",
     "qa_prefix_attn",
     "qa_check_device_error",
+    "qa_ancestor_diagnostics",
     "qa_w4a16_gemm",
     "qa_w4a16_plan",
     "qa_w4a16_dequant",
@@ -111,6 +112,8 @@ def lib() -> ctypes.CDLL:
         L.qa_prefix_attn.restype = c_int
         L.qa_check_device_error.argtypes = [POINTER(c_int)]
         L.qa_check_device_error.restype = c_int
+        L.qa_ancestor_diagnostics.argtypes = [POINTER(c_int32)]
+        L.qa_ancestor_diagnostics.restype = c_int
         L.qa_w4a16_gemm.argtypes = [POINTER(W4A16Args), c_void_p]
         L.qa_w4a16_gemm.restype = c_int
         L.qa_w4a16_gemm_noalloc.argtypes = [POINTER(W4A16Args), c_void_p]
@@ -149,3 +152,10 @@ def check(status: int, what: str) -> None:
 
 def i64_array(vals) -> ctypes.Array:
     return (c_int64 * len(vals))(*[int(v) for v in vals])
+
+
+def ancestor_diagnostics() -> list:
+    """Read and clear the ancestor kernel's first failed plan check (8 ints; [0] == 0: none)."""
+    out = (c_int32 * 8)()
+    check(lib().qa_ancestor_diagnostics(out), "qa_ancestor_diagnostics")
+    return list(out)

@@ -33,11 +33,20 @@
 // host plans every tile's capacity), for head_dim 64, 128 and 256; chains and
 // explicit parents take the scalar walk.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "ancestor_plan.cuh"
 
 namespace qa {
+
+// First failed plan check of the tensor-core ancestor kernel since the last
+// read: [0] check (1 sizes, 2 query row, 3 key slot, 4 staged row), [1] tile,
+// [2] sequence, [3] offending value, [4] plan from the table, [5] sequence
+// length, [6] tile rows, [7] staged rows. Read and cleared by
+// qa_ancestor_diagnostics; [0] also sets bit 4 of qa_check_device_error.
+__device__ int g_anc_diag[8];
+
 namespace {
 
 constexpr int kWarps = 4;
@@ -56,6 +65,38 @@ struct TcParams {
   int32_t num_sms;     // host-side launch planning only
   int32_t unit_heads;  // > 0: CTA x runs unit x = (tile, chunk of unit_heads heads)
   FastDiv div_b;
+  // Tile-plan table (plans of a full-length tree, one record per tile; see
+  // TilePlanRec): read when plan != nullptr, or written (and nothing else
+  // done) by a launch with plan_out = 1 and one CTA per tile.
+  uint32_t* plan;
+  int32_t plan_stride;  // words per record
+  uint32_t plan_key;    // word 0 of a valid record of this launch's table
+  int32_t plan_out;
+};
+
+// One tile's plan in the table (32-bit words): [0] key, [1] plan_tile_word, [2] rows of
+// the tile, [3] staged K/V rows, [4 + w] warp w's rows | key columns << 16,
+// [8 + r] tree node of tile row r, [72 + 64 w + c / 2] staged slot of warp w's
+// key column c (16 bits each), [328 + 2 t + h] thread t's walk-key mask of its
+// row g + 8 h, [584 + j] tree node of staged row j.
+// Record check words: a table assignment's key is a well-mixed 32-bit value
+// and word 1 mixes it with the tile index, so stale words of an earlier table
+// in the same slot (node numbers, masks, small counts) do not pass for a record.
+__host__ __device__ inline uint32_t plan_mix(uint32_t x) {  // a 32-bit finaliser (MurmurHash3 fmix32)
+  x ^= x >> 16;
+  x *= 0x85ebca6bu;
+  x ^= x >> 13;
+  x *= 0xc2b2ae35u;
+  x ^= x >> 16;
+  return x;
+}
+__host__ __device__ inline uint32_t plan_tile_word(uint32_t key, int tile) {
+  return plan_mix(key ^ (0x9e3779b9u * uint32_t(tile + 1)));
+}
+
+struct TilePlanRec {
+  static constexpr int kRows = 8, kSlots = 72, kSel = 328, kStaged = 584;
+  static int words(int rows_cap) { return (kStaged + rows_cap + 3) & ~3; }
 };
 
 QA_DEVINL uint32_t smem_u32(const void* p) {
@@ -156,6 +197,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   __shared__ int w_col[kWarps][kMaxLevels];       // contiguous tiles: column = w_col[s] + node, per warp
   __shared__ int w_levels[kWarps];
   __shared__ int kslot[kWarps][kTcMaxKeys];       // staged K/V row of each key column
+  __shared__ bool table_hit;                      // this tile's plan is in the table
 
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a following GEMM may stage
   const qa_ancestor_args& a = p.a;
@@ -175,6 +217,12 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
     it_end = items * (blockIdx.x + 1) / gridDim.x;
   }
   bool waited = false;  // griddepcontrol.wait done (before the first global read)
+  if (p.plan_out) {  // planning launch: CTA x plans tile x of a full-length tree
+    it = int64_t(blockIdx.x) * a.num_q_heads;
+    it_end = it + 1;
+  }
+  bool from_table = false;  // this tile's plan came from the table
+  const uint32_t* rec = nullptr;
   while (it < it_end) {
   const int64_t tg = it / a.num_q_heads;
   const int h_first = int(it - tg * a.num_q_heads);
@@ -213,7 +261,42 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   wn = 0;
   sel0 = sel1 = 0u;
   nkeys = kpad = 0;
-  if constexpr (SUB) {
+  from_table = false;
+  if (p.plan != nullptr && !p.plan_out && len_plan == a.max_seqlen) {
+    // a full-length tree: its tile plans are in the table when the record's
+    // key matches this launch's. One thread reads the key (the record may be
+    // written while this CTA runs) and the barrier hands its answer, and the
+    // visibility of the record it guards, to every thread.
+    rec = p.plan + int64_t(tile) * p.plan_stride;
+    if (tid == 0) {
+      uint32_t k0;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(k0) : "l"(rec) : "memory");
+      table_hit = k0 == p.plan_key && __ldcg(rec + 1) == plan_tile_word(p.plan_key, tile);
+    }
+    __syncthreads();
+    if (table_hit) {
+      from_table = true;
+      nq = min(int(__ldcg(rec + 2)), kTcMQ);
+      nrows = min(int(__ldcg(rec + 3)), p.rows_cap);
+      const uint32_t wk = __ldcg(rec + 4 + warp);
+      wn = min(int(wk & 0xffffu), 16);
+      nkeys = min(int(wk >> 16), p.kw_cap);
+      kpad = (nkeys + 15) & ~15;
+      if (SUB && tid < kTcMQ) q_node[tid] = int(__ldcg(rec + TilePlanRec::kRows + tid));
+      const uint32_t* sl = rec + TilePlanRec::kSlots + warp * (kTcMaxKeys / 2);
+      for (int c = lane; c < kTcMaxKeys; c += 32) {
+        const uint32_t w2 = __ldcg(sl + c / 2);
+        kslot[warp][c] = min(int((c & 1) ? (w2 >> 16) : (w2 & 0xffffu)), p.rows_cap - 1);
+      }
+      sel0 = __ldcg(rec + TilePlanRec::kSel + 2 * tid);
+      sel1 = __ldcg(rec + TilePlanRec::kSel + 2 * tid + 1);
+      q_lo = SUB ? 0 : tile * kTcMQ;
+      __syncthreads();  // q_node and the key slots are visible
+    }
+  }
+  if (from_table) {
+    // planned: nothing to compute
+  } else if constexpr (SUB) {
     // ---- plans, shared by every head: the tile's staged windows (thread 1)
     // and each warp's key windows (lane 0 of each warp), computed in parallel ----
     if (tid == 0) n_seg = tile_segments(p.geom, tile, len_plan, seg_lo, seg_row);
@@ -263,7 +346,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       __syncthreads();
     }
   }
-  if (nq > 0) {
+  if (nq > 0 && !from_table) {
     nw = n_win;
     nrows = win_base[nw];
     // key column -> staged slot (columns past the list repeat its last row)
@@ -327,6 +410,34 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       }
     }
   }
+  if (p.plan_out) {  // write this tile's record (no input is read) and stop
+    uint32_t* out = p.plan + int64_t(tile) * p.plan_stride;
+    if (tid < kTcMQ) out[TilePlanRec::kRows + tid] = uint32_t(tid < nq ? row_tok(tid) : 0);
+    if (tid == 0) {
+      out[2] = uint32_t(nq);
+      out[3] = uint32_t(nrows);
+    }
+    if (lane == 0) out[4 + warp] = uint32_t(wn) | (uint32_t(nkeys) << 16);
+    for (int c = 2 * lane; c < kTcMaxKeys; c += 64) {
+      const uint32_t lo = c < kpad ? uint32_t(kslot[warp][c]) : 0u;
+      const uint32_t hi = c + 1 < kpad ? uint32_t(kslot[warp][c + 1]) : 0u;
+      out[TilePlanRec::kSlots + warp * (kTcMaxKeys / 2) + c / 2] = lo | (hi << 16);
+    }
+    out[TilePlanRec::kSel + 2 * tid] = sel0;
+    out[TilePlanRec::kSel + 2 * tid + 1] = sel1;
+    for (int j = tid; j < nrows; j += kTcThreads) {
+      int w = 0;
+      while (w + 1 < nw && win_base[w + 1] <= j) ++w;
+      out[TilePlanRec::kStaged + j] = uint32_t(win_lo[w] + (j - win_base[w]));
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      out[1] = plan_tile_word(p.plan_key, tile);
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(out), "r"(p.plan_key) : "memory");
+    }
+    return;
+  }
   if (waited) break;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // inputs of the previous kernel are visible
   waited = true;
@@ -337,10 +448,53 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   len_plan = len;  // a shorter sequence: plan again
   }  // plan passes
   if (nq == 0) continue;  // uniform over the CTA
+  {
+    // Plan check: every row and key the tile will address lies inside its
+    // sequence and its staged rows. A plan that fails (which the planner
+    // should never produce) is recorded in the device diagnostics and the tile
+    // is skipped instead of reading or writing out of bounds.
+    int bad = 0, val = 0;
+    if (nq > kTcMQ || nrows > p.rows_cap || kpad > p.kw_cap || wn > 16) bad = 1, val = nq;
+    if (!bad && tid < nq) {
+      const int r = row_tok(tid);
+      if (r < 0 || r >= len) bad = 2, val = r;
+    }
+    if (!bad && wn > 0)
+      for (int c = lane; c < kpad; c += 32)
+        if (kslot[warp][c] < 0 || kslot[warp][c] >= nrows) bad = 3, val = kslot[warp][c];
+    for (int j = tid; !bad && j < nrows; j += kTcThreads) {
+      int node;
+      if (from_table) {
+        node = int(__ldcg(rec + TilePlanRec::kStaged + j));
+      } else {
+        int w = 0;
+        while (w + 1 < nw && win_base[w + 1] <= j) ++w;
+        node = win_lo[w] + (j - win_base[w]);
+      }
+      if (node < 0 || node >= len) bad = 4, val = node;
+    }
+    if (__syncthreads_or(bad != 0)) {
+      if (bad && atomicCAS(&g_anc_diag[0], 0, bad) == 0) {
+        g_anc_diag[1] = tile;
+        g_anc_diag[2] = seq;
+        g_anc_diag[3] = val;
+        g_anc_diag[4] = from_table ? 1 : 0;
+        g_anc_diag[5] = len;
+        g_anc_diag[6] = nq;
+        g_anc_diag[7] = nrows;
+      }
+      continue;
+    }
+  }
   for (int j = tid; j < nrows; j += kTcThreads) {  // byte offset of every staged row
-    int w = 0;
-    while (w + 1 < nw && win_base[w + 1] <= j) ++w;
-    const int node = win_lo[w] + (j - win_base[w]);
+    int node;
+    if (from_table) {
+      node = min(int(__ldcg(rec + TilePlanRec::kStaged + j)), len - 1);
+    } else {
+      int w = 0;
+      while (w + 1 < nw && win_base[w + 1] <= j) ++w;
+      node = win_lo[w] + (j - win_base[w]);
+    }
     if (a.page_table == nullptr) {
       const int64_t tk = int64_t(kv0) + node;
       row_off[2 * j] = tk * a.k_stride_t * int64_t(sizeof(T));
@@ -645,8 +799,104 @@ int resident_ctas(int smem) {
 // Launched with programmatic stream serialisation: the kernel may start while
 // the previous kernel on the stream finishes; it plans its first tile, then
 // waits (griddepcontrol.wait) before its first read of any input.
+// Tile-plan tables: kPlanSlots tables of kPlanSlotWords words in a fixed
+// device array (no allocation). A table holds every tile's plan of one tree
+// shape (branching, depth, length) and is filled once by a planning launch;
+// each record carries the key of its table's assignment, so a launch whose
+// key does not match (the slot was reassigned) plans on the device instead.
+constexpr int kPlanSlots = 4;
+constexpr int64_t kPlanSlotWords = int64_t(128) << 10;  // 512 KB per table
+__device__ __align__(16) uint32_t g_tile_plans[kPlanSlots * kPlanSlotWords];
+
+struct PlanSlot {
+  int dev = -1, b = 0, d = 0, n = 0, sub = 0, rows_cap = 0, kw_cap = 0;
+  uint32_t key = 0;
+  uint64_t last_use = 0;
+};
+
 template <typename T, int D, int NBK, int MINB, bool SUB>
-int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st) {
+int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st, bool pdl = true);
+
+// Table of this tree shape on the current device, planned on first use with a
+// launch on `st` ahead of the attention launch (not while `st` is being
+// captured: a captured planning launch would only run when the graph does).
+// Returns false when the plans do not fit a table; p.plan stays null then.
+// The registry of table assignments: one for the whole library (every kernel
+// instantiation shares the tables), keyed by device and tree shape.
+struct PlanRegistry {
+  std::mutex mu;
+  PlanSlot slots[kQaMaxDevices][kPlanSlots];
+  uint32_t* base[kQaMaxDevices] = {nullptr};
+  uint32_t gen[kQaMaxDevices] = {0};
+  uint64_t clock = 0;
+};
+PlanRegistry& plan_registry() {
+  static PlanRegistry r;
+  return r;
+}
+
+// Table of this tree shape on the current device, planned on first use with a
+// launch on `st` ahead of the attention launch (not while `st` is being
+// captured: a captured planning launch would only run when the graph does).
+// Returns false when the plans do not fit a table; p.plan stays null then.
+template <typename T, int D, int NBK, int MINB, bool SUB>
+bool attach_plan_table(TcParams& p, int smem, cudaStream_t st) {
+  p.plan = nullptr;
+  p.plan_out = 0;
+  static const bool disabled = [] {  // QA_TILE_PLAN_TABLES=0 plans every tile on the device
+    const char* e = std::getenv("QA_TILE_PLAN_TABLES");
+    return e != nullptr && e[0] == '0';
+  }();
+  if (disabled) return false;
+  const int stride = TilePlanRec::words(p.rows_cap);
+  if (int64_t(p.geom.tiles) * stride > kPlanSlotWords) return false;
+  const int dev = qa_current_device();
+  PlanRegistry& R = plan_registry();
+  std::lock_guard<std::mutex> lock(R.mu);
+  if (R.base[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_tile_plans) != cudaSuccess || ptr == nullptr) return false;
+    R.base[dev] = static_cast<uint32_t*>(ptr);
+  }
+  PlanSlot* slots = R.slots[dev];
+  PlanSlot* hit = nullptr;
+  for (int i = 0; i < kPlanSlots; ++i) {
+    const PlanSlot& sl = slots[i];
+    if (sl.key != 0 && sl.b == p.a.branching && sl.d == p.a.max_depth && sl.n == p.a.max_seqlen &&
+        sl.sub == int(SUB) && sl.rows_cap == p.rows_cap && sl.kw_cap == p.kw_cap)
+      hit = &slots[i];
+  }
+  if (hit == nullptr) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
+    hit = &slots[0];  // a free slot, else the least recently used one
+    for (int i = 0; i < kPlanSlots; ++i)
+      if (slots[i].key == 0 || slots[i].last_use < hit->last_use) hit = &slots[i];
+    uint32_t key = 0;
+    while (key == 0) key = plan_mix(++R.gen[dev] * 0x9e3779b9u + uint32_t(dev) * 0x7f4a7c15u + 0x6a09e667u);
+    TcParams q = p;
+    q.plan = R.base[dev] + int64_t(hit - slots) * kPlanSlotWords;
+    q.plan_stride = stride;
+    q.plan_key = key;
+    q.plan_out = 1;
+    q.unit_heads = 0;
+    hit->key = 0;  // invalid until the planning launch is queued
+    // Clear the slot first: the new records do not cover every word of the old
+    // ones (different record strides, unwritten tails), and a launch captured
+    // in a graph while the old table was valid must find no intact old record.
+    if (cudaMemsetAsync(q.plan, 0, size_t(kPlanSlotWords) * sizeof(uint32_t), st) != cudaSuccess) return false;
+    if (launch_tc<T, D, NBK, MINB, SUB>(q, p.geom.tiles, smem, st, false) != QA_OK) return false;
+    *hit = PlanSlot{dev, p.a.branching, p.a.max_depth, p.a.max_seqlen, int(SUB), p.rows_cap, p.kw_cap, key, 0};
+  }
+  hit->last_use = ++R.clock;
+  p.plan = R.base[dev] + int64_t(hit - slots) * kPlanSlotWords;
+  p.plan_stride = stride;
+  p.plan_key = hit->key;
+  return true;
+}
+
+template <typename T, int D, int NBK, int MINB, bool SUB>
+int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(blocks));
   cfg.blockDim = dim3(kTcThreads);
@@ -656,7 +906,7 @@ int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   if (cudaLaunchKernelEx(&cfg, ancestor_tc_kernel<T, D, NBK, MINB, SUB>, p) != cudaSuccess) return QA_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
@@ -680,6 +930,10 @@ int launch_tc_minb(TcParams& p, cudaStream_t st) {
     if (occ4 > occ) occ = occ4, minb = 4;
   }
   if (occ <= 0) return QA_ERR_LAUNCH;
+  bool table = false;
+  if (minb == 4) table = attach_plan_table<T, D, NBK, 4, SUB>(p, smem, st);
+  else if (minb == 3) table = attach_plan_table<T, D, NBK, 3, SUB>(p, smem, st);
+  else table = attach_plan_table<T, D, NBK, 1, SUB>(p, smem, st);
   int64_t blocks = min(items, int64_t(p.num_sms) * occ);
   // Work split. A tile's plan costs about as much as kPlanHeads heads (the
   // subtree planner more), so an even split of the (tile, head) items, whose
@@ -687,7 +941,8 @@ int launch_tc_minb(TcParams& p, cudaStream_t st) {
   // unit per CTA when every unit gets a slot; the cheaper estimate wins.
   p.unit_heads = 0;
   {
-    const double plan = SUB ? 2.0 : 1.2;  // tile plan cost in heads (measured)
+    // tile plan cost in heads (measured); a plan read from the table costs little
+    const double plan = table ? 0.3 : (SUB ? 2.0 : 1.2);
     const int H = p.a.num_q_heads;
     const int64_t tgs = int64_t(p.a.batch) * p.geom.tiles;
     const double even = double((items + blocks - 1) / blocks) + 2.0 * plan;
@@ -793,6 +1048,10 @@ int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
   p.kw_cap = plan.kw_cap;
   p.num_sms = qa_sm_count();
   p.div_b = make_fast_div(uint32_t(a.branching));
+  p.plan = nullptr;
+  p.plan_stride = 0;
+  p.plan_key = 0;
+  p.plan_out = 0;
   const bool bf = a.dtype == QA_DTYPE_BF16;
   switch (a.head_dim) {
     case 64: return bf ? launch_tc_nbk<__nv_bfloat16, 64>(p, st) : launch_tc_nbk<__half, 64>(p, st);
@@ -802,3 +1061,22 @@ int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
 }
 
 }  // namespace qa
+
+namespace qa {
+// 1 when a plan check has failed since the last qa_ancestor_diagnostics, -1 on error.
+int ancestor_diag_pending() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_anc_diag, sizeof(int)) != cudaSuccess) return -1;
+  return v != 0 ? 1 : 0;
+}
+}  // namespace qa
+
+extern "C" int qa_ancestor_diagnostics(int32_t* out8) {
+  using namespace qa;
+  int v[8] = {0}, zero[8] = {0};
+  if (cudaMemcpyFromSymbol(v, g_anc_diag, sizeof(v)) != cudaSuccess) return QA_ERR_LAUNCH;
+  if (v[0] != 0 && cudaMemcpyToSymbol(g_anc_diag, zero, sizeof(zero)) != cudaSuccess) return QA_ERR_LAUNCH;
+  if (out8 != nullptr)
+    for (int i = 0; i < 8; ++i) out8[i] = v[i];
+  return QA_OK;
+}

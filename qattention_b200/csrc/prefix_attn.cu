@@ -480,6 +480,7 @@ extern "C" int qa_prefix_attn(const qa_prefix_args* args, void* stream) {
 
 namespace qa {
 int w4a16_read_clear_error();  // w4a16_gemm.cu
+int ancestor_diag_pending();           // ancestor_tc.cu
 }
 
 extern "C" int qa_check_device_error(int* flag) {
@@ -490,6 +491,8 @@ extern "C" int qa_check_device_error(int* flag) {
     return QA_ERR_LAUNCH;
   const int w = qa::w4a16_read_clear_error();
   if (w < 0) return QA_ERR_LAUNCH;
-  *flag = v | w;
+  const int d0 = qa::ancestor_diag_pending();
+  if (d0 < 0) return QA_ERR_LAUNCH;
+  *flag = v | w | (d0 != 0 ? 4 : 0);
   return QA_OK;
 }

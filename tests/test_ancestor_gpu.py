@@ -271,6 +271,41 @@ def test_cuda_graph_capture():
     assert torch.equal(out, ref)
 
 
+def test_tile_plan_tables_reassigned_under_a_captured_graph():
+    # Tile plans of a full-length tree shape live in a small set of tables inside
+    # the library; a graph captured while one shape's table was valid must stay
+    # correct after other shapes take the tables over (its launches then plan on
+    # the device), and shorter sequences (planned on the device) must agree too.
+    H, D = 4, 64
+    shapes = [(2, 7), (3, 4), (4, 3), (2, 8), (5, 3), (2, 6)]
+    runs = []
+    for i, (b, d) in enumerate(shapes):
+        N = tm.num_tree_nodes(b, d)
+        lens = [N, N - 5, N]  # the middle sequence is shorter than max_seqlen
+        qs, ks, vs = ([torch.randn(n, H, D, generator=torch.Generator().manual_seed(1000 * k + 10 * i + j)).half()
+                       for j, n in enumerate(lens)] for k in range(3))
+        Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+        runs.append((b, d, N, lens, qs, ks, vs, Q.cuda(), K.cuda(), V.cuda(), cu))
+    b, d, N, lens, qs, ks, vs, Q, K, V, cu = runs[0]
+    first = ra.ragged_attention(Q, K, V, cu, b, d)
+    cud = cu.cuda()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = ra.ragged_attention(Q, K, V, cud, b, d, max_seqlen=N)
+    for b2, d2, N2, lens2, qs2, ks2, vs2, Q2, K2, V2, cu2 in runs[1:]:  # the tables change hands
+        O2 = ra.ragged_attention(Q2, K2, V2, cu2, b2, d2)
+        ref2 = torch.cat(orc.padded_sdpa(qs2, ks2, vs2, [orc.ancestor_mask(n, b2, d2) for n in lens2]), 0)
+        assert torch.allclose(O2.float().cpu(), ref2, atol=ATOL, rtol=RTOL)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
+    ref = torch.cat(orc.padded_sdpa(qs, ks, vs, [orc.ancestor_mask(n, b, d) for n in lens]), 0)
+    assert torch.allclose(first.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+    assert torch.equal(ra.ragged_attention(Q, K, V, cu, b, d), first)
+    from qattention_b200 import _lib
+    assert _lib.ancestor_diagnostics()[0] == 0  # every plan the kernel used passed its checks
+
+
 @pytest.mark.parametrize("lens,d,H", [([511, 300, 130, 511, 64, 1], 8, 32), ([511, 511, 255, 400], 5, 32),
                                       ([1023, 700, 129], 9, 4)])
 def test_deep_trees_ragged_subtree_tiles(lens, d, H):
