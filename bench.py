@@ -433,6 +433,61 @@ def measure_prefix(dev, steps, warmup):
     return res
 
 
+def measure_parents(dev, steps, warmup):
+    """Explicit-parent trees (``ragged_attention_with_parents``, the reference's E2E verify call):
+    the C2 batch given as parent arrays, and a C2-sized batch of EAGLE-style pruned trees
+    (8 trees of ~1365 nodes, b=8, d=5); algorithmic GB/s as for the headline."""
+    import numpy as np
+    from qattention_b200 import ragged_attn as ra
+    from qattention_b200 import tree_mask as tm
+    H, D, B = 32, 128, 8
+    out = {}
+    for name, b, d, pruned in (("C2_as_parents", 4, 5, False), ("C2_sized_pruned_b8_d5", 8, 5, True)):
+        rng = np.random.default_rng(77)
+        trees = [tm.build_pruned_tree(b, d, target_nodes=1365, rng=rng) if pruned else tm.build_tree(b, d)
+                 for _ in range(B)]
+        lens = [len(t) for t in trees]
+        T = sum(lens)
+        g = torch.Generator().manual_seed(78)
+        Qh, Kh, Vh = (torch.randn(T, H, D, generator=g).half() for _ in range(3))
+        cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+        par = torch.from_numpy(np.concatenate([tm.kernel_parents(t) for t in trees])).to(dev)
+        nbytes = algorithmic_bytes(T, H, D)
+        copies, ins = _rotating(Qh, Kh, Vh, dev, nbytes)
+        cud = cu.to(dev)
+        ms_len = max(lens)
+
+        def step(i):
+            ra.ragged_attention_with_parents(*ins[i % copies], cud, par, d, max_seqlen=ms_len)
+
+        run = graph_steps(step, copies, dev)
+        ms = time_run(run, steps, warmup, dev)
+        del run
+        # the same trees planned once (as every layer of a verify step can share)
+        plan = ra.plan_parents(cud, par, d, max_seqlen=ms_len)
+
+        def step_planned(i):
+            ra.ragged_attention_with_parents(*ins[i % copies], cud, par, d, max_seqlen=ms_len, plan=plan)
+
+        run = graph_steps(step_planned, copies, dev)
+        ms_planned = time_run(run, steps, warmup, dev)
+        O, L = ra.ragged_attention_with_parents(*ins[0], cud, par, d, max_seqlen=ms_len)
+        from oracle import tree_attn_oracle as orc
+        sl = slice(0, lens[0])
+        ro, rl = orc.sparse_ancestor_attention(Qh[sl, :4], Kh[sl, :4], Vh[sl, :4], [0, lens[0]], 0, d,
+                                               parents=par[sl].cpu(), dtype=torch.float32)
+        err = float((O[sl, :4].float().cpu() - ro).abs().max())
+        peak, kind = _peaks()
+        out[name] = {"us_per_step": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                     "frac": nbytes / (ms * 1e-3) / 1e9 / peak, "tokens": T, "algorithmic_bytes": nbytes,
+                     "plan_reused": {"us_per_step": ms_planned * 1e3, "gbs": nbytes / (ms_planned * 1e-3) / 1e9,
+                                     "frac": nbytes / (ms_planned * 1e-3) / 1e9 / peak},
+                     "check_tree0_4heads_max_abs_err": err,
+                     "launches_per_step": 2, "kernels": "ancestor_parents_plan_kernel + ancestor_tc_kernel"}
+        del run, ins
+    return out
+
+
 def measure_hybrid(dev, steps, warmup):
     """Config 4 whole verify attention: tcgen05 prefix pass + ancestor pass with the LSE merge fused."""
     from qattention_b200 import ragged_attn as ra
@@ -745,6 +800,7 @@ def run_ours(args):
                 cfg: time_triton_reference(cfg, dev, args.steps, args.warmup, (O, L)),
                 other: time_triton_reference(other, dev, args.steps, args.warmup, ours_other)}
             torch.cuda.empty_cache()
+            secondary["explicit_parents"] = measure_parents(dev, args.steps, args.warmup)
             secondary["C4_prefix"] = measure_prefix(dev, max(args.steps, 10), args.warmup)
             secondary["C4_verify_attention"] = measure_hybrid(dev, max(args.steps, 10), args.warmup)
             torch.cuda.empty_cache()
@@ -822,6 +878,10 @@ def run_kernel_arm(args):
                 "higher_is_better": True, "ms_per_step": v["us_per_layer"] * 1e-3,
                 "roofline": {"bound": "hbm", "achieved": v["weight_gbs"], "peak": r["hbm_peak"], "unit": "GB/s",
                              "frac": v["hbm_frac"], "peak_kind": r["hbm_peak_kind"]}, "detail": r}
+    elif args.kernel == "parents":
+        r = measure_parents(dev, args.steps, args.warmup)
+        line = {"metric": "explicit-parent ancestor attention GB/s (C2-sized pruned batch)",
+                "value": r["C2_sized_pruned_b8_d5"]["gbs"], "unit": "GB/s", "higher_is_better": True, "detail": r}
     elif args.kernel == "verify":
         r = measure_verify(ws, rank, dev, args.steps, args.warmup, args.verify_layers)
         line = {"metric": "W4A16 verify-step tokens/s", "value": r.get("tokens_per_s"), "unit": "tokens/s",
@@ -857,7 +917,7 @@ def main():
     ap.add_argument("--no-secondary", dest="secondary", action="store_false",
                     help="headline only (no C2/C4/C5/W4A16/Triton measurements)")
     ap.add_argument("--kernel", default="ancestor",
-                    choices=["ancestor", "prefix", "hybrid", "w4a16", "verify", "triton"])
+                    choices=["ancestor", "prefix", "hybrid", "w4a16", "verify", "triton", "parents"])
     ap.add_argument("--verify-layers", type=int, default=0, help="override the layer count (tests only)")
     ap.add_argument("--w4-m", default="16,64,1023,8184", help="token counts of the w4a16 measurement")
     args = ap.parse_args()

@@ -108,9 +108,28 @@ typedef struct qa_ancestor_args {
   int64_t k_stride_page, v_stride_page;  /* paged K/V: elements between pages */
   int32_t page_size;            /* paged K/V: tokens per page */
   int64_t q_stride_b;           /* 0: packed query rows; else batch stride (see above) */
+  void* workspace;              /* explicit parents: plan scratch (see below), optional */
+  int64_t workspace_bytes;
+  int32_t workspace_planned;    /* 1: workspace already holds the plans of these parents */
 } qa_ancestor_args;
 
 QA_API int qa_ancestor_attn(const qa_ancestor_args* args, void* stream);
+
+/*
+ * Explicit parents on tensor cores (ragged_attention_with_parents, the
+ * reference's _ragged_attn_parents_kernel_lse, src/ragged_attn.py:593-795):
+ * with parents != NULL and a device workspace of at least *bytes (16-byte
+ * aligned) in args->workspace / workspace_bytes, qa_ancestor_attn plans every
+ * (sequence, 64-query tile) from parents[] in a first kernel and runs the
+ * tensor-core tiles on those plans; without it (or when *bytes is 0: head_dim
+ * not 64/128/256, sequences over 16384 tokens, walks over 31 steps) it runs the
+ * per-query walk. The plans depend on cu_seqlens_q, parents, max_depth,
+ * max_seqlen and batch only: qa_ancestor_plan writes them alone, and a call with
+ * workspace_planned = 1 reuses them (e.g. every layer of one verify step, which
+ * share the draft tree) instead of planning again.
+ */
+QA_API int qa_ancestor_workspace_bytes(const qa_ancestor_args* args, int64_t* bytes);
+QA_API int qa_ancestor_plan(const qa_ancestor_args* args, void* stream);
 
 /*
  * Two-way log-sum-exp merge. Replaces fused_lse_merge

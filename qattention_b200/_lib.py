@@ -26,6 +26,8 @@ EXPORTED = (
     "qa_prefix_attn",
     "qa_check_device_error",
     "qa_ancestor_diagnostics",
+    "qa_ancestor_workspace_bytes",
+    "qa_ancestor_plan",
     "qa_w4a16_gemm",
     "qa_w4a16_plan",
     "qa_w4a16_dequant",
@@ -57,6 +59,7 @@ class AncestorArgs(Structure):
         ("page_table", c_void_p), ("page_table_stride", c_int64),
         ("k_stride_page", c_int64), ("v_stride_page", c_int64), ("page_size", c_int32),
         ("q_stride_b", c_int64),
+        ("workspace", c_void_p), ("workspace_bytes", c_int64), ("workspace_planned", c_int32),
     ]
 
 
@@ -114,6 +117,10 @@ def lib() -> ctypes.CDLL:
         L.qa_check_device_error.restype = c_int
         L.qa_ancestor_diagnostics.argtypes = [POINTER(c_int32)]
         L.qa_ancestor_diagnostics.restype = c_int
+        L.qa_ancestor_workspace_bytes.argtypes = [POINTER(AncestorArgs), POINTER(c_int64)]
+        L.qa_ancestor_workspace_bytes.restype = c_int
+        L.qa_ancestor_plan.argtypes = [POINTER(AncestorArgs), c_void_p]
+        L.qa_ancestor_plan.restype = c_int
         L.qa_w4a16_gemm.argtypes = [POINTER(W4A16Args), c_void_p]
         L.qa_w4a16_gemm.restype = c_int
         L.qa_w4a16_gemm_noalloc.argtypes = [POINTER(W4A16Args), c_void_p]

@@ -72,6 +72,11 @@ struct TcParams {
   int32_t plan_stride;  // words per record
   uint32_t plan_key;    // word 0 of a valid record of this launch's table
   int32_t plan_out;
+  // Explicit parents: per-call plans, one record per (sequence, tile), written
+  // by ancestor_parents_plan_kernel just before this launch (read after the
+  // programmatic-launch wait). Warps flagged in a record's word 1 ("walk warps")
+  // attend their rows with a per-row walk over global memory instead.
+  const uint32_t* par_plan;
 };
 
 // One tile's plan in the table (32-bit words): [0] key, [1] plan_tile_word, [2] rows of
@@ -170,10 +175,102 @@ template <int D> struct TcSmem {
   __host__ __device__ static int total(int rows) { return tok_off(rows) + rows * 16 + 128; }
 };
 
+// Per-row walk of one warp over global memory (explicit-parent tiles whose
+// key lists do not fit the staged rows): rows [node_lo, node_lo + n) of
+// sequence `seq`, query head h. Lanes split head_dim (D/32 elements each);
+// the walk follows parents[] as the scalar kernel does (ends at a self-loop,
+// a parent outside the sequence, or max_depth steps); exact online softmax in
+// fp32 with the prefix result (if any) merged in as one extra key.
+template <typename T, int D>
+__device__ __noinline__ void walk_rows(const TcParams& p, int h, int seq, int q0, int len, int kv0, int node_lo,
+                                       int n, int lane) {
+  constexpr int E = D / 32;  // elements per lane (2, 4 or 8)
+  const qa_ancestor_args& a = p.a;
+  const int hk = h / p.head_ratio;
+  auto load = [&](const void* base, int64_t elem_off, float (&f)[E]) {
+    const T* src = reinterpret_cast<const T*>(base) + elem_off + lane * E;
+#pragma unroll
+    for (int i = 0; i < E / 2; ++i) {
+      const float2 v = pair_to_f32<T>(__ldg(reinterpret_cast<const unsigned int*>(src) + i));
+      f[2 * i] = v.x;
+      f[2 * i + 1] = v.y;
+    }
+  };
+  auto kv_off = [&](int node, int64_t& ko, int64_t& vo) {
+    if (a.page_table == nullptr) {
+      const int64_t tk = int64_t(kv0) + node;
+      ko = tk * a.k_stride_t;
+      vo = tk * a.v_stride_t;
+    } else {
+      const int pos = a.kv_offset + node;
+      const int64_t page = __ldg(a.page_table + int64_t(seq) * a.page_table_stride + pos / a.page_size);
+      ko = page * a.k_stride_page + int64_t(pos % a.page_size) * a.k_stride_t;
+      vo = page * a.v_stride_page + int64_t(pos % a.page_size) * a.v_stride_t;
+    }
+    ko += int64_t(hk) * a.k_stride_h;
+    vo += int64_t(hk) * a.v_stride_h;
+  };
+  for (int i = 0; i < n; ++i) {
+    const int q = node_lo + i;
+    const int64_t t = int64_t(q0) + q;
+    float qf[E], acc[E];
+    load(a.q, q_seq_off(a, seq, q0) + int64_t(q) * a.q_stride_t + int64_t(h) * a.q_stride_h, qf);
+    float m = -INFINITY, l = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    if (a.prefix_o != nullptr) {
+      const float pl = __ldg(a.prefix_lse + t * a.prefix_lse_stride_t + int64_t(h) * a.prefix_lse_stride_h);
+      if (pl > -INFINITY) {
+        load(a.prefix_o, t * a.prefix_o_stride_t + int64_t(h) * a.prefix_o_stride_h, acc);
+        m = pl * kLog2e;
+        l = 1.f;
+      }
+    }
+    int node = q;
+    for (int s = 0;; ++s) {
+      int64_t ko, vo;
+      kv_off(node, ko, vo);
+      float kf[E], vf[E];
+      load(a.k, ko, kf);
+      load(a.v, vo, vf);
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) d = fmaf(qf[e], kf[e], d);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      const float sc = d * p.scale_log2;
+      if (sc > m) {
+        const float alpha = fast_exp2(m - sc);
+        l *= alpha;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] *= alpha;
+        m = sc;
+      }
+      const float w = fast_exp2(sc - m);
+      l += w;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = fmaf(w, vf[e], acc[e]);
+      if (s >= a.max_depth) break;
+      const int nx = __ldg(a.parents + q0 + node);
+      if (nx == node || nx < 0 || nx >= len) break;
+      node = nx;
+    }
+    const float inv = 1.f / l;
+    T* o = reinterpret_cast<T*>(a.o) + t * a.o_stride_t + int64_t(h) * a.o_stride_h + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e += 2)
+      *reinterpret_cast<uint32_t*>(o + e) = pack2<T>(acc[e] * inv, acc[e + 1] * inv);
+    if (a.lse != nullptr && lane == 0)
+      a.lse[t * a.lse_stride_t + int64_t(h) * a.lse_stride_h] = (m + __log2f(l)) * kLn2;
+  }
+}
+
 // MINB = CTAs per SM the register allocation must allow (1, 3 or 4; chosen
 // per launch by launch_tc_minb).
-template <typename T, int D, int NBK, int MINB, bool SUB>
+template <typename T, int D, int NBK, int MINB, int MODE>
 __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcParams p) {
+  constexpr bool SUB = MODE == 1;  // subtree tiles
+  constexpr bool PAR = MODE == 2;  // explicit parents: per-call plans, walk warps
   using SM = TcSmem<D>;
   constexpr int RC = D / 8;   // 16-byte chunks per row
   constexpr int KB = D / 16;  // k16 steps of q.k
@@ -246,6 +343,7 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   }
   int len_plan = waited ? len : a.max_seqlen;
   int q_lo = 0, nq = 0, wn = 0, nw = 0, nrows = 0, nkeys = 0, kpad = 0;
+  int walk_n = 0;  // explicit parents: rows of this warp attended by walk_rows
   uint32_t sel0 = 0u, sel1 = 0u;  // walk-key masks, the same for every head
   // token (relative to the sequence) of tile row r
   auto row_tok = [&](int r) -> int {
@@ -262,6 +360,39 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
   sel0 = sel1 = 0u;
   nkeys = kpad = 0;
   from_table = false;
+  if constexpr (PAR) {
+    // explicit parents: the plan kernel wrote this (sequence, tile)'s record
+    // just before this launch, so read it after the programmatic-launch wait
+    if (!waited) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      waited = true;
+      q0 = __ldg(a.cu_seqlens_q + seq);
+      len = __ldg(a.cu_seqlens_q + seq + 1) - q0;
+      kv0 = (a.cu_seqlens_kv ? __ldg(a.cu_seqlens_kv + seq) : q0) + a.kv_offset;
+    }
+    rec = p.par_plan + (int64_t(seq) * p.geom.tiles + tile) * p.plan_stride;
+    nq = min(int(__ldcg(rec + 2)), kTcMQ);
+    nrows = min(int(__ldcg(rec + 3)), p.rows_cap);
+    const uint32_t wk = __ldcg(rec + 4 + warp);
+    wn = min(int(wk & 0xffffu), 16);
+    nkeys = min(int(wk >> 16), p.kw_cap);
+    if ((__ldcg(rec + 1) >> warp) & 1u) {  // a walk warp: no key list, rows go to walk_rows
+      walk_n = wn;
+      wn = nkeys = 0;
+    }
+    kpad = (nkeys + 15) & ~15;
+    const uint32_t* sl = rec + TilePlanRec::kSlots + warp * (kTcMaxKeys / 2);
+    for (int c = lane; c < kTcMaxKeys; c += 32) {
+      const uint32_t w2 = __ldcg(sl + c / 2);
+      kslot[warp][c] = min(int((c & 1) ? (w2 >> 16) : (w2 & 0xffffu)), p.rows_cap - 1);
+    }
+    sel0 = __ldcg(rec + TilePlanRec::kSel + 2 * tid);
+    sel1 = __ldcg(rec + TilePlanRec::kSel + 2 * tid + 1);
+    q_lo = tile * kTcMQ;
+    from_table = true;
+    __syncthreads();  // the key slots are visible
+    break;
+  }
   if (p.plan != nullptr && !p.plan_out && len_plan == a.max_seqlen) {
     // a full-length tree: its tile plans are in the table when the record's
     // key matches this launch's. One thread reads the key (the record may be
@@ -764,14 +895,223 @@ __global__ void __launch_bounds__(kTcThreads, MINB) ancestor_tc_kernel(const TcP
       if (g + 8 < wn) *reinterpret_cast<uint32_t*>(orow1 + 8 * j) = pack2<T>(o[j][2], o[j][3]);
     }
   }
+  if constexpr (PAR) {
+    if (walk_n > 0) walk_rows<T, D>(p, h, seq, q0, len, kv0, q_lo + wrow, walk_n, lane);
+  }
   if (next) issue_v(h + 1); else cp_async_commit();
   }  // heads
   }  // tiles
 }
 
+// ---------------------------------------------------------------------------
+// Explicit-parent plans (one CTA of 128 threads per (sequence, tile of 64
+// consecutive BFS nodes)). Each row's walk follows parents[] exactly as the
+// per-query kernel does; the walk nodes of each warp's 16 rows form its key
+// list and the union over the warps is the tile's staged row set, both in
+// ascending node order via bitmaps over the sequence's nodes (kParWords words).
+// A warp whose key list exceeds the key columns, or whose keys would push the
+// union past the staged rows, becomes a walk warp (walk_rows). Writes one
+// TilePlanRec per (sequence, tile); word 1 holds the walk-warp mask.
+// ---------------------------------------------------------------------------
+constexpr int kParMaxSeq = 16384;          // nodes per sequence the plans cover
+constexpr int kParWords = kParMaxSeq / 32;  // bitmap words
+constexpr int kParRowsCap = 96;            // staged rows of a parents tile
+constexpr int kParKeys = 64;               // key columns per warp (deep walks)
+
+struct ParPlanSmem {
+  uint32_t cta_bm[kParWords];
+  uint32_t warp_bm[kWarps][kParWords];
+  int cta_pref[kParWords];
+  int warp_pref[kWarps][kParWords];
+  int walk[kTcMQ][kMaxLevels];
+  int walk_len[kTcMQ];
+  int kcol[kWarps][kTcMaxKeys];
+  int red[kWarps];
+};
+
+__global__ void __launch_bounds__(kTcThreads) ancestor_parents_plan_kernel(const qa_ancestor_args a, int tiles,
+                                                                            int stride, int rows_cap, int kw_cap,
+                                                                            uint32_t* __restrict__ plans) {
+  extern __shared__ __align__(16) unsigned char par_smem[];
+  ParPlanSmem& S = *reinterpret_cast<ParPlanSmem*>(par_smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int seq = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // parents / cu_seqlens may come from the previous kernel
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  uint32_t* out = plans + (int64_t(seq) * tiles + tile) * stride;
+  const int q0 = __ldg(a.cu_seqlens_q + seq);
+  const int len = min(__ldg(a.cu_seqlens_q + seq + 1) - q0, kParMaxSeq);
+  const int q_lo = tile * kTcMQ;
+  const int nq = max(0, min(kTcMQ, len - q_lo));
+  if (nq == 0) {
+    if (tid == 0) out[1] = out[2] = out[3] = 0u;
+    if (tid < kWarps) out[4 + tid] = 0u;
+    return;
+  }
+  const int words = (len + 31) / 32;
+  // the sequence's parents, staged once (the walks then chase them in shared memory)
+  int* par_s = reinterpret_cast<int*>(par_smem + sizeof(ParPlanSmem));
+  for (int i = tid; i < len; i += kTcThreads) par_s[i] = __ldg(a.parents + q0 + i);
+  for (int i = tid; i < words; i += kTcThreads) {
+    S.cta_bm[i] = 0u;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) S.warp_bm[w][i] = 0u;
+  }
+  __syncthreads();
+  const int levels = min(a.max_depth + 1, kMaxLevels);
+  if (tid < nq) {  // row tid's walk
+    int n = q_lo + tid, s = 0;
+    for (;;) {
+      S.walk[tid][s] = n;
+      atomicOr(&S.warp_bm[tid >> 4][n >> 5], 1u << (n & 31));
+      if (s + 1 >= levels) break;
+      const int nx = par_s[n];
+      if (nx == n || nx < 0 || nx >= len) break;
+      n = nx;
+      ++s;
+    }
+    S.walk_len[tid] = s + 1;
+  }
+  __syncthreads();
+  // key-list sizes per warp, then the union, warp by warp while it fits
+  uint32_t walk_mask = 0u;
+  int nkeys[kWarps];
+  int nrows = 0;
+  for (int w = 0; w < kWarps; ++w) {
+    int own = 0, uni = 0;
+    for (int i = tid; i < words; i += kTcThreads) {
+      own += __popc(S.warp_bm[w][i]);
+      uni += __popc(S.warp_bm[w][i] | S.cta_bm[i]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      own += __shfl_xor_sync(0xffffffffu, own, off);
+      uni += __shfl_xor_sync(0xffffffffu, uni, off);
+    }
+    if (lane == 0) S.red[warp] = own | (uni << 16);
+    __syncthreads();
+    own = uni = 0;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) {
+      own += S.red[i] & 0xffff;
+      uni += S.red[i] >> 16;
+    }
+    nkeys[w] = own;
+    const bool rows_w = q_lo + w * 16 < q_lo + nq;
+    if (rows_w && own <= kw_cap && uni <= rows_cap) {
+      for (int i = tid; i < words; i += kTcThreads) S.cta_bm[i] |= S.warp_bm[w][i];
+      nrows = uni;
+    } else if (rows_w) {
+      walk_mask |= 1u << w;
+    }
+    __syncthreads();
+  }
+  // exclusive popcount prefixes: the CTA bitmap by all threads (one word each
+  // per pass, pass totals carried), each good warp's bitmap by that warp
+  {
+    int carry = 0;
+    for (int base = 0; base < words; base += kTcThreads) {
+      const int i = base + tid;
+      const int c = i < words ? __popc(S.cta_bm[i]) : 0;
+      int x = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+      }
+      if (lane == 31) S.red[warp] = x;
+      __syncthreads();
+      int before = carry;
+      for (int w = 0; w < warp; ++w) before += S.red[w];
+      if (i < words) S.cta_pref[i] = before + x - c;
+      for (int w = 0; w < kWarps; ++w) carry += S.red[w];
+      __syncthreads();
+    }
+  }
+  if (!((walk_mask >> warp) & 1u)) {
+    int carry = 0;
+    for (int base = 0; base < words; base += 32) {
+      const int i = base + lane;
+      const int c = i < words ? __popc(S.warp_bm[warp][i]) : 0;
+      int x = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+      }
+      if (i < words) S.warp_pref[warp][i] = carry + x - c;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+  }
+  __syncthreads();
+  auto cta_slot = [&](int n) {
+    return S.cta_pref[n >> 5] + __popc(S.cta_bm[n >> 5] & ((1u << (n & 31)) - 1u));
+  };
+  auto warp_col = [&](int w, int n) {
+    return S.warp_pref[w][n >> 5] + __popc(S.warp_bm[w][n >> 5] & ((1u << (n & 31)) - 1u));
+  };
+  // staged rows in ascending node order
+  for (int i = tid; i < words; i += kTcThreads) {
+    uint32_t bits = S.cta_bm[i];
+    int slot = S.cta_pref[i];
+    while (bits) {
+      const int b = __ffs(bits) - 1;
+      bits &= bits - 1u;
+      out[TilePlanRec::kStaged + slot++] = uint32_t(32 * i + b);
+    }
+  }
+  // key columns -> staged slots (padded columns repeat the last key)
+  const bool good = !((walk_mask >> warp) & 1u);
+  if (good) {
+    for (int i = lane; i < words; i += 32) {
+      uint32_t bits = S.warp_bm[warp][i];
+      int col = S.warp_pref[warp][i];
+      while (bits) {
+        const int b = __ffs(bits) - 1;
+        bits &= bits - 1u;
+        S.kcol[warp][col++] = cta_slot(32 * i + b);
+      }
+    }
+  }
+  __syncwarp();
+  const int nk = good ? nkeys[warp] : 0;
+  const int kp = (nk + 15) & ~15;
+  for (int c = 2 * lane; c < kTcMaxKeys; c += 64) {
+    const uint32_t lo = c < kp ? uint32_t(S.kcol[warp][min(c, nk - 1)]) : 0u;
+    const uint32_t hi = c + 1 < kp ? uint32_t(S.kcol[warp][min(c + 1, nk - 1)]) : 0u;
+    out[TilePlanRec::kSlots + warp * (kTcMaxKeys / 2) + c / 2] = lo | (hi << 16);
+  }
+  // walk-key masks: thread (g, t) of the warp owns column c of rows g and g + 8
+  // in block c / 8, element c % 2, when (c % 8) / 2 == t
+  uint32_t sel[2] = {0u, 0u};
+  const int g = lane >> 2, t = lane & 3;
+  if (good) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = warp * 16 + g + 8 * half;
+      if (r >= nq) continue;
+      for (int s2 = 0; s2 < S.walk_len[r]; ++s2) {
+        const int c = warp_col(warp, S.walk[r][s2]);
+        if (((c >> 1) & 3) == t) sel[half] |= 1u << (((c >> 3) << 1) | (c & 1));
+      }
+    }
+  }
+  out[TilePlanRec::kSel + 2 * tid] = sel[0];
+  out[TilePlanRec::kSel + 2 * tid + 1] = sel[1];
+  if (lane == 0) {
+    const int wn = max(0, min(16, nq - warp * 16));
+    out[4 + warp] = uint32_t(wn) | (uint32_t(nk) << 16);
+  }
+  if (tid == 0) {
+    out[1] = walk_mask;
+    out[2] = uint32_t(nq);
+    out[3] = uint32_t(nrows);
+  }
+}
+
 // Resident CTAs per SM of one instantiation at this shared-memory size
 // (memoised: the size depends only on the tree shape).
-template <typename T, int D, int NBK, int MINB, bool SUB>
+template <typename T, int D, int NBK, int MINB, int MODE>
 int resident_ctas(int smem) {
   // (smem << 32 | occupancy) of the last query on each device; atomic so that
   // host threads launching concurrently read a consistent pair
@@ -784,11 +1124,11 @@ int resident_ctas(int smem) {
   const int64_t m = memo[dev].load(std::memory_order_relaxed);
   if (m >= 0 && int(m >> 32) == smem) return int(m & 0xffffffff);
   {
-    if (qa_smem_attr(reinterpret_cast<const void*>(ancestor_tc_kernel<T, D, NBK, MINB, SUB>), kTcMaxSmem) !=
+    if (qa_smem_attr(reinterpret_cast<const void*>(ancestor_tc_kernel<T, D, NBK, MINB, MODE>), kTcMaxSmem) !=
         cudaSuccess)
       return 0;
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ancestor_tc_kernel<T, D, NBK, MINB, SUB>, kTcThreads,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ancestor_tc_kernel<T, D, NBK, MINB, MODE>, kTcThreads,
                                                       smem) != cudaSuccess)
       return 0;
     memo[dev].store((int64_t(smem) << 32) | int64_t(occ), std::memory_order_relaxed);
@@ -814,7 +1154,7 @@ struct PlanSlot {
   uint64_t last_use = 0;
 };
 
-template <typename T, int D, int NBK, int MINB, bool SUB>
+template <typename T, int D, int NBK, int MINB, int MODE>
 int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st, bool pdl = true);
 
 // Table of this tree shape on the current device, planned on first use with a
@@ -839,10 +1179,11 @@ PlanRegistry& plan_registry() {
 // launch on `st` ahead of the attention launch (not while `st` is being
 // captured: a captured planning launch would only run when the graph does).
 // Returns false when the plans do not fit a table; p.plan stays null then.
-template <typename T, int D, int NBK, int MINB, bool SUB>
+template <typename T, int D, int NBK, int MINB, int MODE>
 bool attach_plan_table(TcParams& p, int smem, cudaStream_t st) {
   p.plan = nullptr;
   p.plan_out = 0;
+  if (p.par_plan != nullptr) return false;  // explicit parents carry their own per-call plans
   static const bool disabled = [] {  // QA_TILE_PLAN_TABLES=0 plans every tile on the device
     const char* e = std::getenv("QA_TILE_PLAN_TABLES");
     return e != nullptr && e[0] == '0';
@@ -863,7 +1204,7 @@ bool attach_plan_table(TcParams& p, int smem, cudaStream_t st) {
   for (int i = 0; i < kPlanSlots; ++i) {
     const PlanSlot& sl = slots[i];
     if (sl.key != 0 && sl.b == p.a.branching && sl.d == p.a.max_depth && sl.n == p.a.max_seqlen &&
-        sl.sub == int(SUB) && sl.rows_cap == p.rows_cap && sl.kw_cap == p.kw_cap)
+        sl.sub == MODE && sl.rows_cap == p.rows_cap && sl.kw_cap == p.kw_cap)
       hit = &slots[i];
   }
   if (hit == nullptr) {
@@ -885,8 +1226,8 @@ bool attach_plan_table(TcParams& p, int smem, cudaStream_t st) {
     // ones (different record strides, unwritten tails), and a launch captured
     // in a graph while the old table was valid must find no intact old record.
     if (cudaMemsetAsync(q.plan, 0, size_t(kPlanSlotWords) * sizeof(uint32_t), st) != cudaSuccess) return false;
-    if (launch_tc<T, D, NBK, MINB, SUB>(q, p.geom.tiles, smem, st, false) != QA_OK) return false;
-    *hit = PlanSlot{dev, p.a.branching, p.a.max_depth, p.a.max_seqlen, int(SUB), p.rows_cap, p.kw_cap, key, 0};
+    if (launch_tc<T, D, NBK, MINB, MODE>(q, p.geom.tiles, smem, st, false) != QA_OK) return false;
+    *hit = PlanSlot{dev, p.a.branching, p.a.max_depth, p.a.max_seqlen, MODE, p.rows_cap, p.kw_cap, key, 0};
   }
   hit->last_use = ++R.clock;
   p.plan = R.base[dev] + int64_t(hit - slots) * kPlanSlotWords;
@@ -895,7 +1236,7 @@ bool attach_plan_table(TcParams& p, int smem, cudaStream_t st) {
   return true;
 }
 
-template <typename T, int D, int NBK, int MINB, bool SUB>
+template <typename T, int D, int NBK, int MINB, int MODE>
 int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(blocks));
@@ -907,7 +1248,7 @@ int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st, bool pdl) 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, ancestor_tc_kernel<T, D, NBK, MINB, SUB>, p) != cudaSuccess) return QA_ERR_LAUNCH;
+  if (cudaLaunchKernelEx(&cfg, ancestor_tc_kernel<T, D, NBK, MINB, MODE>, p) != cudaSuccess) return QA_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_LAUNCH;
 }
 
@@ -917,23 +1258,23 @@ int launch_tc(TcParams& p, int64_t blocks, int smem, cudaStream_t st, bool pdl) 
 // they raise residency; at equal residency the build with more registers runs
 // faster. head_dim 256 is held to <= 2 CTAs by shared memory and uses the
 // unconstrained build only.
-template <typename T, int D, int NBK, bool SUB>
+template <typename T, int D, int NBK, int MODE>
 int launch_tc_minb(TcParams& p, cudaStream_t st) {
   const int64_t items = int64_t(p.a.batch) * p.geom.tiles * p.a.num_q_heads;
   const int smem = TcSmem<D>::total(p.rows_cap);
-  const int occ1 = resident_ctas<T, D, NBK, 1, SUB>(smem);
+  const int occ1 = resident_ctas<T, D, NBK, 1, MODE>(smem);
   int occ = occ1, minb = 1;
   if constexpr (D <= 128) {
-    const int occ3 = resident_ctas<T, D, NBK, 3, SUB>(smem);
-    const int occ4 = resident_ctas<T, D, NBK, 4, SUB>(smem);
+    const int occ3 = resident_ctas<T, D, NBK, 3, MODE>(smem);
+    const int occ4 = resident_ctas<T, D, NBK, 4, MODE>(smem);
     if (occ3 > occ) occ = occ3, minb = 3;
     if (occ4 > occ) occ = occ4, minb = 4;
   }
   if (occ <= 0) return QA_ERR_LAUNCH;
   bool table = false;
-  if (minb == 4) table = attach_plan_table<T, D, NBK, 4, SUB>(p, smem, st);
-  else if (minb == 3) table = attach_plan_table<T, D, NBK, 3, SUB>(p, smem, st);
-  else table = attach_plan_table<T, D, NBK, 1, SUB>(p, smem, st);
+  if (minb == 4) table = attach_plan_table<T, D, NBK, 4, MODE>(p, smem, st);
+  else if (minb == 3) table = attach_plan_table<T, D, NBK, 3, MODE>(p, smem, st);
+  else table = attach_plan_table<T, D, NBK, 1, MODE>(p, smem, st);
   int64_t blocks = min(items, int64_t(p.num_sms) * occ);
   // Work split. A tile's plan costs about as much as kPlanHeads heads (the
   // subtree planner more), so an even split of the (tile, head) items, whose
@@ -942,7 +1283,7 @@ int launch_tc_minb(TcParams& p, cudaStream_t st) {
   p.unit_heads = 0;
   {
     // tile plan cost in heads (measured); a plan read from the table costs little
-    const double plan = table ? 0.3 : (SUB ? 2.0 : 1.2);
+    const double plan = (table || MODE == 2) ? 0.3 : (MODE == 1 ? 2.0 : 1.2);
     const int H = p.a.num_q_heads;
     const int64_t tgs = int64_t(p.a.batch) * p.geom.tiles;
     const double even = double((items + blocks - 1) / blocks) + 2.0 * plan;
@@ -959,14 +1300,15 @@ int launch_tc_minb(TcParams& p, cudaStream_t st) {
     if (p.unit_heads > 0) blocks = tgs * ((H + p.unit_heads - 1) / p.unit_heads);
   }
   if (blocks <= 0) return QA_OK;
-  if (minb == 4) return launch_tc<T, D, NBK, 4, SUB>(p, blocks, smem, st);
-  if (minb == 3) return launch_tc<T, D, NBK, 3, SUB>(p, blocks, smem, st);
-  return launch_tc<T, D, NBK, 1, SUB>(p, blocks, smem, st);
+  if (minb == 4) return launch_tc<T, D, NBK, 4, MODE>(p, blocks, smem, st);
+  if (minb == 3) return launch_tc<T, D, NBK, 3, MODE>(p, blocks, smem, st);
+  return launch_tc<T, D, NBK, 1, MODE>(p, blocks, smem, st);
 }
 
 template <typename T, int D, int NBK>
 int launch_tc_sub(TcParams& p, cudaStream_t st) {
-  return p.geom.bands > 0 ? launch_tc_minb<T, D, NBK, true>(p, st) : launch_tc_minb<T, D, NBK, false>(p, st);
+  if (p.par_plan != nullptr) return launch_tc_minb<T, D, NBK, 2>(p, st);
+  return p.geom.bands > 0 ? launch_tc_minb<T, D, NBK, 1>(p, st) : launch_tc_minb<T, D, NBK, 0>(p, st);
 }
 
 template <typename T, int D>
@@ -1029,8 +1371,76 @@ bool tc_plan(int b, int max_depth, int n, TcPlan& out) {
   return memo_ok;
 }
 
+// Explicit parents on the tensor-core kernel: the per-call plans need the
+// caller's workspace (qa_ancestor_workspace_bytes); 0 when the path does not
+// apply (head_dim, sequence length, walk depth).
+int64_t parents_workspace_bytes(const qa_ancestor_args& a) {
+  if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return 0;
+  if (a.max_seqlen <= 0 || a.max_seqlen > kParMaxSeq || a.max_depth + 1 > kMaxLevels || a.batch <= 0) return 0;
+  const int tiles = (a.max_seqlen + kTcMQ - 1) / kTcMQ;
+  return int64_t(a.batch) * tiles * TilePlanRec::words(kParRowsCap) * int64_t(sizeof(uint32_t));
+}
+
+// Explicit-parent plans of every (sequence, tile) into a.workspace.
+int launch_parents_plan(const qa_ancestor_args& a, int tiles, int stride, int kw_cap, cudaStream_t st) {
+  const int smem = int(sizeof(ParPlanSmem)) + a.max_seqlen * int(sizeof(int));
+  if (qa_smem_attr(reinterpret_cast<const void*>(ancestor_parents_plan_kernel), smem) != cudaSuccess)
+    return QA_ERR_LAUNCH;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(int64_t(a.batch) * tiles));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, ancestor_parents_plan_kernel, a, tiles, stride, int(kParRowsCap), kw_cap,
+                         static_cast<uint32_t*>(a.workspace)) != cudaSuccess)
+    return QA_ERR_LAUNCH;
+  return QA_OK;
+}
+
+int ancestor_tc_parents_launch(const qa_ancestor_args& a, cudaStream_t st, bool plan_only = false) {
+  const int64_t need = parents_workspace_bytes(a);
+  if (need == 0 || a.workspace == nullptr || a.workspace_bytes < need ||
+      (reinterpret_cast<uintptr_t>(a.workspace) & 15u))
+    return kTcNotApplicable;
+  TcParams p;
+  p.a = a;
+  p.scale_log2 = a.scale * kLog2e;
+  p.geom = make_tile_geom(2, a.max_seqlen, false);
+  p.head_ratio = a.num_q_heads / a.num_kv_heads;
+  p.rows_cap = kParRowsCap;
+  // key columns per warp: 32 (four S blocks) for shallow trees, whose 16 rows
+  // rarely have more walk keys (rows that do go to walk warps), 64 for deeper
+  // ones; four blocks run ~15 % faster than eight on C2-sized batches
+  p.kw_cap = a.max_depth <= 6 ? 32 : kParKeys;
+  p.num_sms = qa_sm_count();
+  p.div_b = make_fast_div(2u);
+  p.plan = nullptr;
+  p.plan_key = 0;
+  p.plan_out = 0;
+  p.plan_stride = TilePlanRec::words(kParRowsCap);
+  p.par_plan = static_cast<const uint32_t*>(a.workspace);
+  // plans first (programmatic launch: it waits for the previous kernel before
+  // reading parents), then the attention launch reads them after its own wait;
+  // workspace_planned = 1: the workspace already holds these plans
+  if (a.workspace_planned == 0 || plan_only) {
+    const int st_plan = launch_parents_plan(a, int(p.geom.tiles), int(p.plan_stride), int(p.kw_cap), st);
+    if (st_plan != QA_OK || plan_only) return st_plan;
+  }
+  const bool bf = a.dtype == QA_DTYPE_BF16;
+  switch (a.head_dim) {
+    case 64: return bf ? launch_tc_nbk<__nv_bfloat16, 64>(p, st) : launch_tc_nbk<__half, 64>(p, st);
+    case 128: return bf ? launch_tc_nbk<__nv_bfloat16, 128>(p, st) : launch_tc_nbk<__half, 128>(p, st);
+    default: return bf ? launch_tc_nbk<__nv_bfloat16, 256>(p, st) : launch_tc_nbk<__half, 256>(p, st);
+  }
+}
+
 int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
-  if (a.parents != nullptr) return kTcNotApplicable;
+  if (a.parents != nullptr) return ancestor_tc_parents_launch(a, st);
   if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return kTcNotApplicable;
   if (a.branching < 2 || a.max_seqlen <= 0) return kTcNotApplicable;  // chains: the scalar walk
   TcPlan plan;
@@ -1052,6 +1462,7 @@ int ancestor_tc_launch(const qa_ancestor_args& a, cudaStream_t st) {
   p.plan_stride = 0;
   p.plan_key = 0;
   p.plan_out = 0;
+  p.par_plan = nullptr;
   const bool bf = a.dtype == QA_DTYPE_BF16;
   switch (a.head_dim) {
     case 64: return bf ? launch_tc_nbk<__nv_bfloat16, 64>(p, st) : launch_tc_nbk<__half, 64>(p, st);
@@ -1079,4 +1490,17 @@ extern "C" int qa_ancestor_diagnostics(int32_t* out8) {
   if (out8 != nullptr)
     for (int i = 0; i < 8; ++i) out8[i] = v[i];
   return QA_OK;
+}
+
+extern "C" int qa_ancestor_workspace_bytes(const qa_ancestor_args* args, int64_t* bytes) {
+  if (args == nullptr || bytes == nullptr) return QA_ERR_INVALID;
+  *bytes = args->parents != nullptr ? qa::parents_workspace_bytes(*args) : 0;
+  return QA_OK;
+}
+
+extern "C" int qa_ancestor_plan(const qa_ancestor_args* args, void* stream) {
+  using namespace qa;
+  if (args == nullptr || args->parents == nullptr || args->cu_seqlens_q == nullptr) return QA_ERR_INVALID;
+  const int r = ancestor_tc_parents_launch(*args, reinterpret_cast<cudaStream_t>(stream), true);
+  return r == kTcNotApplicable ? QA_ERR_UNSUPPORTED : r;
 }

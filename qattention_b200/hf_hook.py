@@ -76,7 +76,19 @@ def _tree_attention(module, query, key, value, attention_mask, scaling=None, dro
     parents = st.get("tree_parents")
     if flag is not None and flag.get("tree_parents") is not None:
         parents = flag["tree_parents"]
-    out = tree_verify_attention(query, key, value, st["branching"], st["max_depth"], tree_parents=parents)
+    plan = None
+    if parents is not None:
+        # every layer of the step shares the tree: plan its tiles once (per tensor and version)
+        from .ragged_attn import plan_tree_parents
+        B, N = query.shape[0], query.shape[2]
+        pk = (id(parents), parents._version, B, N, str(query.device))
+        plans = st.setdefault("plans", {})
+        if pk not in plans:
+            plans.clear()
+            plans[pk] = plan_tree_parents(parents, B, st["max_depth"], device=query.device)
+        plan = plans[pk]
+    out = tree_verify_attention(query, key, value, st["branching"], st["max_depth"], tree_parents=parents,
+                                plan=plan)
     st["stats"]["n"] += 1
     return out.transpose(1, 2), None  # [B, N, Hq, D] (contiguous underneath)
 

@@ -18,6 +18,7 @@ Reference entry points mirrored here (file:line in the reference project):
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import List, Optional, Tuple
 
@@ -100,7 +101,7 @@ def pack_inputs(
 
 def _ancestor(Q, K, V, cu_dev, max_seqlen, *, branching=1, max_depth=0, parents=None,
               want_lse=False, cu_kv=None, kv_offset=0, prefix_o=None, prefix_lse=None,
-              out=None, lse_out=None, q_batched=None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+              out=None, lse_out=None, q_batched=None, plan=None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Launch ``qa_ancestor_attn`` on torch's current stream; returns (O, LSE or None).
 
     ``q_batched``: the queries as a ``[B, N, Hq, D]`` view read in place through its
@@ -146,6 +147,16 @@ def _ancestor(Q, K, V, cu_dev, max_seqlen, *, branching=1, max_depth=0, parents=
     a.kv_offset, a.branching, a.max_depth, a.max_seqlen = kv_offset, branching, max_depth, max_seqlen
     a.scale = 1.0 / math.sqrt(D)
     a.dtype = _dtype_code(Q.dtype)
+    ws = None
+    if plan is not None:  # plans made once for these parents (plan_parents)
+        plan._check(B, max_depth, max_seqlen)
+        a.workspace, a.workspace_bytes, a.workspace_planned = plan.workspace.data_ptr(), plan.nbytes, 1
+    elif parents is not None:  # plan scratch of the tensor-core explicit-parent path
+        need = ctypes.c_int64(0)
+        _lib.check(_lib.lib().qa_ancestor_workspace_bytes(a, ctypes.byref(need)), "qa_ancestor_workspace_bytes")
+        if need.value > 0:
+            ws = torch.empty(need.value, dtype=torch.uint8, device=Q.device)
+            a.workspace, a.workspace_bytes = ws.data_ptr(), need.value
     _lib.check(_lib.lib().qa_ancestor_attn(a, _stream_ptr(Q.device)), "qa_ancestor_attn")
     return O, LSE
 
@@ -188,6 +199,55 @@ def ragged_attention_with_lse(
                      want_lse=True)
 
 
+class ParentsPlan:
+    """Tile plans of explicit-parent trees, made once by :func:`plan_parents` and
+    reused by every call on the same trees (e.g. all layers of one verify step).
+
+    Holds the device workspace with the plans, the int32 parents and cu_seqlens
+    they were made from, and the batch, max_depth and max_seqlen they cover.
+    """
+
+    def __init__(self, workspace, nbytes, parents, cu, batch, max_depth, max_seqlen):
+        self.workspace, self.nbytes = workspace, nbytes
+        self.parents, self.cu_seqlens = parents, cu
+        self.batch, self.max_depth, self.max_seqlen = batch, max_depth, max_seqlen
+
+    def _check(self, batch, max_depth, max_seqlen):
+        if (batch, max_depth, max_seqlen) != (self.batch, self.max_depth, self.max_seqlen):
+            raise ValueError(f"plan made for (batch, max_depth, max_seqlen) = "
+                             f"{(self.batch, self.max_depth, self.max_seqlen)}, "
+                             f"called with {(batch, max_depth, max_seqlen)}")
+
+
+def plan_parents(cu_seqlens: torch.Tensor, parents: torch.Tensor, max_depth: int, max_seqlen: int = None,
+                 device=None) -> Optional[ParentsPlan]:
+    """Plans every (sequence, 64-query tile) of explicit-parent trees on the device
+    (one kernel) for reuse by :func:`ragged_attention_with_parents` /
+    :func:`tree_verify_attention` calls with ``plan=``. Returns None when the
+    tensor-core path does not apply (sequences over 16384 tokens, walks over 31
+    steps): those calls then take the per-query walk. The plan stays valid while
+    ``parents`` and ``cu_seqlens`` keep their values.
+    """
+    dev = torch.device(device) if device is not None else parents.device
+    if dev.type != "cuda":
+        raise RuntimeError("plan_parents needs a CUDA device: this library has no CPU path")
+    cu_dev, ms = _cu_and_max(cu_seqlens, max_seqlen, dev)
+    par = parents.to(device=dev, dtype=torch.int32).contiguous()
+    a = _lib.AncestorArgs()
+    a.cu_seqlens_q, a.parents = cu_dev.data_ptr(), par.data_ptr()
+    a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim = int(cu_dev.shape[0]) - 1, 1, 1, 128
+    a.max_depth, a.max_seqlen, a.dtype = max_depth, ms, _lib.QA_DTYPE_F16
+    need = ctypes.c_int64(0)
+    _lib.check(_lib.lib().qa_ancestor_workspace_bytes(a, ctypes.byref(need)), "qa_ancestor_workspace_bytes")
+    if need.value == 0:
+        return None
+    ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), need.value
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().qa_ancestor_plan(a, _stream_ptr(dev)), "qa_ancestor_plan")
+    return ParentsPlan(ws, need.value, par, cu_dev, a.batch, max_depth, ms)
+
+
 def ragged_attention_with_parents(
     Q: torch.Tensor,
     K: torch.Tensor,
@@ -196,6 +256,7 @@ def ragged_attention_with_parents(
     parents: torch.Tensor,
     max_depth: int,
     max_seqlen: int = None,
+    plan: Optional[ParentsPlan] = None,
 ) -> tuple:
     """Ancestor-sparse attention over explicit (pruned / EAGLE-style) trees.
 
@@ -203,13 +264,19 @@ def ragged_attention_with_parents(
     self-loop ``parents[root] = root``. The walk stops at the first self-loop or
     after ``max_depth`` parent steps. A parent outside ``[0, L_i)`` also ends
     the walk (the reference reads out of bounds there). Returns (O, lse).
+    ``plan``: optional :func:`plan_parents` result for these parents (skips planning).
     """
     _check_qkv(Q, K, V)
-    cu_dev, ms = _cu_and_max(cu_seqlens, max_seqlen, Q.device)
-    if parents.shape[0] != Q.shape[0]:
-        raise ValueError(f"parents must have one entry per token ({Q.shape[0]}), got {parents.shape[0]}")
-    par = parents.to(device=Q.device, dtype=torch.int32, non_blocking=True).contiguous()
-    return _ancestor(Q, K, V, cu_dev, ms, parents=par, max_depth=max_depth, want_lse=True)
+    if plan is not None:
+        cu_dev, ms, par = plan.cu_seqlens, plan.max_seqlen, plan.parents
+        if max_seqlen is not None and max_seqlen != ms:
+            raise ValueError(f"plan made for max_seqlen {ms}, called with {max_seqlen}")
+    else:
+        cu_dev, ms = _cu_and_max(cu_seqlens, max_seqlen, Q.device)
+        par = parents.to(device=Q.device, dtype=torch.int32, non_blocking=True).contiguous()
+    if par.shape[0] != Q.shape[0]:
+        raise ValueError(f"parents must have one entry per token ({Q.shape[0]}), got {par.shape[0]}")
+    return _ancestor(Q, K, V, cu_dev, ms, parents=par, max_depth=max_depth, want_lse=True, plan=plan)
 
 
 def ragged_attention_paged(
@@ -434,6 +501,7 @@ def tree_verify_attention(
     branching_factor: int,
     max_depth: int,
     tree_parents: Optional[torch.Tensor] = None,
+    plan: Optional[ParentsPlan] = None,
 ) -> torch.Tensor:
     """Verify-step attention in the E2E caller's layout (``_ragged_tree_attn``,
     scripts/w4a16_e2e.py:1201-1309).
@@ -443,7 +511,9 @@ def tree_verify_attention(
     ancestors (complete b-ary BFS tree, or ``tree_parents`` ``[N]`` int32 with
     root self-loop, shared by the batch). Returns ``[B, Hq, N, D]`` (a permuted
     view of a ``[B, N, Hq, D]`` buffer). GQA without ``repeat_kv``; no layout
-    copies of Q/K/V (the kernels take the strides).
+    copies of Q/K/V (the kernels take the strides). ``plan``: a
+    :func:`plan_tree_parents` result for this tree and batch (every layer of a
+    verify step can share it).
     """
     B, Hq, N, D = Q.shape
     Hkv, LN = K.shape[1], K.shape[2]
@@ -456,7 +526,9 @@ def tree_verify_attention(
         out = torch.empty(B, N, Hq, D, dtype=Q.dtype, device=Q.device)
         lse = None
     par = None
-    if tree_parents is not None:
+    if plan is not None:
+        par = plan.parents
+    elif tree_parents is not None:
         par = tree_parents.to(device=Q.device, dtype=torch.int32).repeat(B).contiguous()
     # Queries are read in place: as packed rows when the batch pitch is N token rows (a
     # head slice of a fused qkv projection), else through the kernel's batch stride
@@ -475,8 +547,18 @@ def tree_verify_attention(
               cu_kv=cu_kv, kv_offset=kv_off,
               prefix_o=out.view(B * N, Hq, D) if L > 0 else None,
               prefix_lse=lse.view(B * N, Hq) if L > 0 else None,
-              out=out.view(B * N, Hq, D), q_batched=q_batched)
+              out=out.view(B * N, Hq, D), q_batched=q_batched, plan=plan)
     return out.permute(0, 2, 1, 3)
+
+
+def plan_tree_parents(tree_parents: torch.Tensor, batch: int, max_depth: int, device=None) -> Optional[ParentsPlan]:
+    """:func:`plan_parents` for :func:`tree_verify_attention`: one tree (``tree_parents``
+    ``[N]``, root self-loop) shared by ``batch`` sequences of N queries."""
+    N = int(tree_parents.shape[0])
+    dev = torch.device(device) if device is not None else tree_parents.device
+    cu = torch.arange(0, (batch + 1) * N, N, dtype=torch.int32)
+    par = tree_parents.to(device=dev, dtype=torch.int32).repeat(batch).contiguous()
+    return plan_parents(cu, par, max_depth, max_seqlen=N, device=dev)
 
 
 def _tree_rows(Kt: torch.Tensor, Vt: torch.Tensor, L: int, N: int):

@@ -148,6 +148,91 @@ def test_explicit_parents_pruned_trees(b, d, target, seed):
     assert torch.allclose(L.cpu(), torch.cat(rl, 0), atol=1e-3)
 
 
+@pytest.mark.parametrize("b,d,target,seed,D,dtype", [
+    (8, 5, 1365, 21, 128, torch.float16),   # C2-sized pruned trees: every tile on the key lists
+    (4, 6, 1365, 22, 128, torch.float16),   # tiles past the staged rows: walk warps
+    (3, 7, 1365, 23, 64, torch.float16),
+    (4, 5, 1365, 24, 256, torch.bfloat16),
+    (2, 12, 3000, 25, 128, torch.float16),  # deep walks (13 keys per row)
+])
+def test_explicit_parents_large_pruned_trees(b, d, target, seed, D, dtype):
+    # the reference's E2E verify path (ragged_attention_with_parents on EAGLE-style
+    # pruned trees, scripts/w4a16_e2e.py:1277-1284), at C2-like sizes on the tile path
+    H, B = 8, 3
+    rng = np.random.default_rng(seed)
+    trees = [tm.build_pruned_tree(b, d, target_nodes=target, rng=rng) for _ in range(B)]
+    g = torch.Generator().manual_seed(seed)
+    qs = [torch.randn(len(t), H, D, generator=g).to(dtype) for t in trees]
+    ks = [torch.randn(len(t), H, D, generator=g).to(dtype) for t in trees]
+    vs = [torch.randn(len(t), H, D, generator=g).to(dtype) for t in trees]
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    parents = torch.from_numpy(np.concatenate([tm.kernel_parents(t) for t in trees]))
+    O, L = ra.ragged_attention_with_parents(Q.cuda(), K.cuda(), V.cuda(), cu, parents, d)
+    from qattention_b200 import _lib
+    assert _lib.ancestor_diagnostics()[0] == 0
+    ro, rl = orc.sparse_ancestor_attention(Q, K, V, cu, 0, d, parents=parents, dtype=torch.float32)
+    assert torch.allclose(O.float().cpu(), ro, atol=ATOL, rtol=RTOL)
+    assert torch.allclose(L.cpu(), rl, atol=1e-3)
+    # plans made once and reused give the same bits
+    plan = ra.plan_parents(cu, parents, d, device="cuda")
+    assert plan is not None
+    for _ in range(2):
+        O2, L2 = ra.ragged_attention_with_parents(Q.cuda(), K.cuda(), V.cuda(), cu, parents, d, plan=plan)
+        assert torch.equal(O2, O) and torch.equal(L2, L)
+
+
+def test_explicit_parents_gqa_paged_and_strided():
+    # GQA, a page table and strided query views on the explicit-parent tile path
+    b, d, H, Hkv, D, page = 4, 5, 8, 2, 128, 16
+    rng = np.random.default_rng(31)
+    trees = [tm.build_pruned_tree(b, d, target_nodes=400, rng=rng) for _ in range(3)]
+    lens = [len(t) for t in trees]
+    g = torch.Generator().manual_seed(31)
+    qs = [torch.randn(n, H, D, generator=g).half() for n in lens]
+    ks = [torch.randn(n, Hkv, D, generator=g).half() for n in lens]
+    vs = [torch.randn(n, Hkv, D, generator=g).half() for n in lens]
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    parents = torch.from_numpy(np.concatenate([tm.kernel_parents(t) for t in trees]))
+    Qs = torch.zeros(Q.shape[0], H, 2 * D, dtype=torch.float16)
+    Qs[:, :, :D] = Q
+    O, L = ra.ragged_attention_with_parents(Qs.cuda()[:, :, :D], K.cuda(), V.cuda(), cu, parents, d)
+    rep = H // Hkv
+    ro, rl = orc.sparse_ancestor_attention(Q, K, V, cu, 0, d, parents=parents, dtype=torch.float32)
+    assert torch.allclose(O.float().cpu(), ro, atol=ATOL, rtol=RTOL)
+    # paged K/V through the C ABI: the same plans, rows looked up in the page table
+    Kc, Vc, pt = ra.build_paged_kv(ks, vs, page_size=page)
+    from qattention_b200 import _lib
+    import ctypes, math
+    Qd, Kd, Vd = Q.cuda(), Kc.cuda(), Vc.cuda()
+    Od = torch.empty_like(Qd)
+    ptd, cud, pard = pt.cuda(), cu.cuda(), parents.cuda().int()
+    a = _lib.AncestorArgs()
+    a.q, a.k, a.v, a.o = Qd.data_ptr(), Kd.data_ptr(), Vd.data_ptr(), Od.data_ptr()
+    a.cu_seqlens_q, a.parents = cud.data_ptr(), pard.data_ptr()
+    a.q_stride_t, a.q_stride_h = Qd.stride(0), Qd.stride(1)
+    a.k_stride_t, a.k_stride_h, a.k_stride_page = Kd.stride(1), Kd.stride(2), Kd.stride(0)
+    a.v_stride_t, a.v_stride_h, a.v_stride_page = Vd.stride(1), Vd.stride(2), Vd.stride(0)
+    a.o_stride_t, a.o_stride_h = Od.stride(0), Od.stride(1)
+    a.page_table, a.page_table_stride, a.page_size = ptd.data_ptr(), ptd.stride(0), page
+    a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim = 3, H, Hkv, D
+    a.max_depth, a.max_seqlen, a.scale, a.dtype = d, max(lens), 1.0 / math.sqrt(D), _lib.QA_DTYPE_F16
+    need = ctypes.c_int64(0)
+    assert _lib.lib().qa_ancestor_workspace_bytes(a, ctypes.byref(need)) == 0 and need.value > 0
+    ws = torch.empty(need.value, dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes = ws.data_ptr(), need.value
+    assert _lib.lib().qa_ancestor_attn(a, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert torch.allclose(Od.float().cpu(), ro, atol=ATOL, rtol=RTOL)
+    # without a workspace the per-query walk serves the call: same results within tolerance
+    a.workspace, a.workspace_bytes = None, 0
+    Od2 = torch.empty_like(Qd)
+    a.o = Od2.data_ptr()
+    assert _lib.lib().qa_ancestor_attn(a, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert (Od2.float() - Od.float()).abs().max().item() <= 2e-3
+    assert _lib.ancestor_diagnostics()[0] == 0
+
+
 def test_parents_path_equals_formula_on_complete_tree():
     B, b, d, H, D = 2, 3, 4, 4, 64
     N = tm.num_tree_nodes(b, d)

@@ -114,10 +114,11 @@ def test_struct_layout_matches_header():
         types = {"const", "void", "float", "int32_t", "int64_t"}
         names += [t for t in re.split(r"[\s,*]+", line) if t and t not in types]
     assert names == [f[0] for f in _lib.AncestorArgs._fields_]
-    # 11 pointers and 18 int64 (8 bytes), 10 int32 and a float (4 bytes); the float and the
+    # 12 pointers and 19 int64 (8 bytes), 10 int32 and a float (4 bytes); the float and the
     # int32 dtype pack into one 8-byte slot before the page-table pointer, page_size is
     # padded to 8 before q_stride_b
-    assert ctypes.sizeof(_lib.AncestorArgs) == (11 + 18) * 8 + (10 + 1) * 4 + 4
+    # (workspace_planned, an int32, is padded to 8 at the end)
+    assert ctypes.sizeof(_lib.AncestorArgs) == (12 + 19) * 8 + (10 + 1) * 4 + 4 + 8
 
 
 def test_build_paged_kv_layout():

@@ -109,6 +109,10 @@ def test_tree_verify_attention_e2e_layout(use_parents):
     V = torch.randn(B, Hkv, L + N, D, generator=g).half()
     out = ra.tree_verify_attention(Q.cuda(), K.cuda(), V.cuda(), b, d, tree_parents=parents)
     assert out.shape == (B, Hq, N, D)
+    if use_parents:  # one plan shared by the layers of a verify step: same bits
+        plan = ra.plan_tree_parents(parents, B, d, device="cuda")
+        out2 = ra.tree_verify_attention(Q.cuda(), K.cuda(), V.cuda(), b, d, tree_parents=parents, plan=plan)
+        assert torch.equal(out2, out)
     mask = tm.tree_attention_mask_pruned(tree)
     for s in range(B):
         q = Q[s].permute(1, 0, 2)
