@@ -754,6 +754,9 @@ def ancestor_sharded(cfg, ws, rank, dev, steps, warmup, clocks=None, with_e2e=Tr
                       "what": "each rank: H2D of its trees' Q/K/V from pinned memory, "
                               "sharding.sharded_ragged_attention_with_lse, D2H of O and LSE; bytes summed over ranks"}
     if with_gather:
+        if ws > 1:  # the first gather sets up NCCL's peer connections: warm them up untimed
+            sharding.gather_outputs(O[:1], L[:1], sharding.shard_trees(
+                torch.arange(ws + 1, dtype=torch.int32), ws, rank), dst=0)
         _barrier(ws)
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()

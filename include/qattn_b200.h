@@ -279,6 +279,16 @@ QA_API int qa_silu_mul(const void* gate_up, void* out, int32_t M, int32_t F, voi
 QA_API int qa_check_device_error(int* flag);
 
 /*
+ * Test hook (no counterpart in the reference): the number of polls after which
+ * a pipeline wait of the prefix pass gives up in launches made from now on
+ * (0 restores the default, about a second). A small value makes the waits run
+ * out on purpose, so that a test can see the abort path end the launch, report
+ * through qa_check_device_error, and leave the context usable. The waits that
+ * drain a stopping kernel's own copies and MMAs keep the default limit.
+ */
+QA_API int qa_set_pipeline_wait_limit(uint32_t polls);
+
+/*
  * Diagnostics of the tensor-core ancestor kernel (no counterpart in the
  * reference, whose kernels do not check their index arithmetic): before it
  * stages a tile, the kernel checks that every query row, staged K/V row and key

@@ -28,6 +28,7 @@ EXPORTED = (
     "qa_ancestor_diagnostics",
     "qa_ancestor_workspace_bytes",
     "qa_ancestor_plan",
+    "qa_set_pipeline_wait_limit",
     "qa_w4a16_gemm",
     "qa_w4a16_plan",
     "qa_w4a16_dequant",
@@ -121,6 +122,8 @@ def lib() -> ctypes.CDLL:
         L.qa_ancestor_workspace_bytes.restype = c_int
         L.qa_ancestor_plan.argtypes = [POINTER(AncestorArgs), c_void_p]
         L.qa_ancestor_plan.restype = c_int
+        L.qa_set_pipeline_wait_limit.argtypes = [ctypes.c_uint32]
+        L.qa_set_pipeline_wait_limit.restype = c_int
         L.qa_w4a16_gemm.argtypes = [POINTER(W4A16Args), c_void_p]
         L.qa_w4a16_gemm.restype = c_int
         L.qa_w4a16_gemm_noalloc.argtypes = [POINTER(W4A16Args), c_void_p]

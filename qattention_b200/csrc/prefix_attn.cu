@@ -32,6 +32,8 @@
 //     its in-flight copies and MMAs, frees its TMEM and exits.
 #include "sm100_ptx.cuh"
 
+#include <atomic>
+
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -59,7 +61,12 @@ struct PfxParams {
   int32_t m_tiles;  // per (sequence, kv head)
   int32_t n_tiles;  // key tiles
   float scale_log2;
+  uint32_t wait_limit;  // polls of a pipeline wait before the kernel gives up (kWaitLimit)
 };
+
+// Pipeline-wait limit of the next launches (0 = kWaitLimit): a test hook that
+// makes the bounded waits run out without a fault (qa_set_pipeline_wait_limit).
+std::atomic<uint32_t> g_wait_limit{0};
 
 template <int D> struct PfxSmem {
   static constexpr int Q_BYTES = kBM * D * 2;
@@ -107,7 +114,7 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
   // row out of the 128-byte-swizzled shared tile, so the S MMAs read only K
   // from shared memory ----
   {
-    ok = __all_sync(0xffffffffu, mbar_wait(q_smem_full, 0, abort, kWaitLimit));
+    ok = __all_sync(0xffffffffu, mbar_wait(q_smem_full, 0, abort, p.wait_limit));
     if (!ok) return;
     const int r = warp * 32 + lane;
 #pragma unroll
@@ -126,7 +133,7 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
     if (lane == 0) mbar_arrive(q_tmem_full);
   }
   for (int j = 0; j < ntiles; ++j) {
-    ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort, kWaitLimit));
+    ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort, p.wait_limit));
     if (!ok) break;
     tc_fence_after();
     constexpr int NC = kBN / 32;  // 32-column chunks of the S tile
@@ -157,7 +164,7 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
     const bool need = m_new > m + kLazy;  // always true on the first tile
     if (j > 0 && __any_sync(0xffffffffu, need)) {
       // rescale O in TMEM once P_{j-1} V_{j-1} has landed
-      ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort, kWaitLimit));
+      ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, abort, p.wait_limit));
       if (!ok) break;
       tc_fence_after();
       const float alpha = need ? fast_exp2(m - m_new) : 1.f;
@@ -200,7 +207,7 @@ __device__ __forceinline__ void softmax_role(const PfxParams& p, uint32_t tbase,
     tc_fence_before();
     mbar_arrive(&p_full[j & 1]);
   }
-  if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (ntiles - 1) & 1, abort, kWaitLimit));
+  if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (ntiles - 1) & 1, abort, p.wait_limit));
   if (!ok) return;
   tc_fence_after();
   // ---- epilogue: row -> (token, head); O / l and LSE ----
@@ -299,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % kStages;
-        if (j >= kStages && !mbar_wait(&bar_kv_empty[st], ((j / kStages) - 1) & 1, &abort_flag, kWaitLimit))
+        if (j >= kStages && !mbar_wait(&bar_kv_empty[st], ((j / kStages) - 1) & 1, &abort_flag, p.wait_limit))
           break;
         // K and V of a stage each add their bytes to the stage's barrier (2 arrivals)
         mbar_arrive_expect_tx(&bar_kv_full[st], PfxSmem<D>::KV_BYTES);
@@ -328,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t k_desc0 = sw128_desc(smem_addr(sK(0)), 16, 1024);
       const uint64_t v_desc0 = sw128_desc(smem_addr(sV(0)), kBN * 128, 1024);
       auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(&bar_p_full[i & 1], (i >> 1) & 1, &abort_flag, kWaitLimit)) return false;
+        if (!mbar_wait(&bar_p_full[i & 1], (i >> 1) & 1, &abort_flag, p.wait_limit)) return false;
         tc_fence_after();
         const uint64_t v_desc = v_desc0 + uint64_t((i % kStages) * kStageUnits);
         const uint32_t p_tmem = tbase + (i & 1) * kBN;
@@ -339,11 +346,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&bar_kv_empty[i % kStages]);
         return true;
       };
-      bool ok = mbar_wait(&bar_qt, 0, &abort_flag, kWaitLimit);
+      bool ok = mbar_wait(&bar_qt, 0, &abort_flag, p.wait_limit);
       const uint32_t q_tmem = tbase + 2 * kBN + D;
       for (int j = 0; ok && j < ntiles; ++j) {
         const int st = j % kStages;
-        if (!mbar_wait(&bar_kv_full[st], (j / kStages) & 1, &abort_flag, kWaitLimit)) break;
+        if (!mbar_wait(&bar_kv_full[st], (j / kStages) & 1, &abort_flag, p.wait_limit)) break;
         tc_fence_after();
         const uint64_t k_desc = k_desc0 + uint64_t(st * kStageUnits);
         const uint32_t s_tmem = tbase + (j & 1) * kBN;
@@ -445,6 +452,10 @@ int launch(const qa_prefix_args& a, cudaStream_t st) {
   p.m_tiles = (a.num_queries + kBM / G - 1) / (kBM / G);
   p.n_tiles = (a.prefix_len + kBN - 1) / kBN;
   p.scale_log2 = a.scale * kLog2e;
+  {
+    const uint32_t lim = g_wait_limit.load(std::memory_order_relaxed);
+    p.wait_limit = lim != 0 ? lim : kWaitLimit;
+  }
   const int64_t blocks = int64_t(a.batch) * a.num_kv_heads * p.m_tiles;
   if (blocks > 0x7fffffffLL) return QA_ERR_INVALID;
   if (qa_smem_attr(reinterpret_cast<const void*>(prefix_attn_kernel<T, D>), PfxSmem<D>::TOTAL) != cudaSuccess)
@@ -494,5 +505,10 @@ extern "C" int qa_check_device_error(int* flag) {
   const int d0 = qa::ancestor_diag_pending();
   if (d0 < 0) return QA_ERR_LAUNCH;
   *flag = v | w | (d0 != 0 ? 4 : 0);
+  return QA_OK;
+}
+
+extern "C" int qa_set_pipeline_wait_limit(uint32_t polls) {
+  qa::g_wait_limit.store(polls, std::memory_order_relaxed);
   return QA_OK;
 }
