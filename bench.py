@@ -535,13 +535,15 @@ def measure_w4a16(dev, steps, warmup, ms_list):
         n = max(copies, min(steps, 200 if M <= 1023 else 40))
         ms = _timed_graphs(graphs, n, warmup, dev)
         flops = sum(2.0 * M * K * N for _, _, K, N in layer)
-        launches = 0
-        for _, _, K, N in layer:  # one GEMM, plus the split-K reduce when the plan splits K
+        splits = []
+        for _, _, K, N in layer:  # one launch per GEMM: split-K partials are summed by the last CTA of a tile
             sp, wb = ctypes.c_int32(), ctypes.c_int64()
             _lib.check(_lib.lib().qa_w4a16_plan(M, N, K, ctypes.byref(sp), ctypes.byref(wb)), "qa_w4a16_plan")
-            launches += 1 + (sp.value > 1)
+            splits.append(sp.value)
+        launches = len(layer)
         sweep[str(M)] = {"us_per_layer": ms * 1e3, "weight_gbs": wbytes / (ms * 1e-3) / 1e9,
-                         "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_layer": launches}
+                         "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_layer": launches,
+                         "splits": splits}
         del graphs
     hb, hkind = _peaks()
     tp, tkind = _tensor_peak()

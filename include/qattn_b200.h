@@ -210,6 +210,10 @@ typedef struct qa_w4a16_args {
   int64_t y_stride;
   int32_t M, N, K;
   int32_t splits; /* 0 = automatic */
+  uint32_t* counters; /* optional: (N/128) * ceil(M/16) zeroed counters; with them a split-K
+                         call finishes in one launch (the last CTA of each tile adds the
+                         partials) and leaves them zero; calls that overlap on the GPU
+                         must not share them. NULL: a second kernel adds the partials. */
 } qa_w4a16_args;
 
 QA_API int qa_w4a16_gemm(const qa_w4a16_args* args, void* stream);

@@ -87,6 +87,7 @@ class W4A16Args(Structure):
         ("x", c_void_p), ("qweight", c_void_p), ("scales", c_void_p), ("y", c_void_p),
         ("workspace", c_void_p), ("x_stride", c_int64), ("y_stride", c_int64),
         ("M", c_int32), ("N", c_int32), ("K", c_int32), ("splits", c_int32),
+        ("counters", c_void_p),
     ]
 
 

@@ -115,7 +115,7 @@ __global__ void w4a16_dequant_kernel(const uint32_t* __restrict__ qw, const __ha
 //     the FT feature tiles share every activation stage.
 //   * Epilogue: the dequant warps read the accumulator back (tcgen05.ld).
 // ---------------------------------------------------------------------------
-constexpr int kMaxNA = 6;          // A buffers in TMEM
+constexpr int kMaxNA = 8;          // A buffers in TMEM
 constexpr int kMaxXStages = 10;
 constexpr int kMaxWStages = 10;
 constexpr int kSmem = 216 * 1024;   // dynamic shared memory, one CTA per SM
@@ -130,18 +130,26 @@ struct GemmParams {
   int32_t tn;        // tokens per CTA (MMA N), multiple of 16, <= 256
   int32_t tn_cols;   // TMEM columns per accumulator (tn rounded up to 32)
   int32_t na;        // A buffers
-  int32_t dual;      // two MMA threads (even / odd K steps), one accumulator each
   int32_t x_stages;
   int32_t w_stages;
   int32_t k_tiles_per_split;
+  // split-K finished in the kernel: the last CTA of each (feature, token) tile
+  // to arrive on its counter adds the tile's partial sums into y_out
+  uint32_t* counters;  // nullptr: a separate reduce kernel does it
+  __half* y_out;
+  int64_t y_out_stride;
 };
 
 // CPS = CTAs resident per SM (1 or 2): with 2, each CTA takes half of the
 // TMEM columns and of the shared memory, and two independent pipelines
 // interleave on the SM (the per-step latency chain of one pipeline caps its
 // weight stream well below the SM's share of HBM bandwidth).
-template <int FT, bool SPLIT, int CPS>
-__global__ void __launch_bounds__(96 + FT * 256, CPS)
+// NP producer warps (steps i % NP), NM MMA-issuing warps (steps i % NM, one
+// accumulator each) and NG dequant groups of 4 FT warps (steps i % NG): at
+// small M each role's barrier round trips, not any unit's throughput, set
+// the pace, so several independent chains per role raise the weight stream.
+template <int FT, bool SPLIT, int CPS, int NG, int NM, int NP>
+__global__ void __launch_bounds__(32 * (NP + NM) + NG * FT * 128, CPS)
     w4a16_gemm_kernel(const __grid_constant__ CUtensorMap x_map, const GemmParams p) {
   using namespace sm100;
   constexpr int kWBytesFT = FT * kWBytes;     // packed weights of one step
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
       mbar_init(&bar_w_empty[s], FT * 4);  // one arrival per warp of the step's dequant group
     }
     for (int b = 0; b < NA; ++b) mbar_init(&bar_a_empty[b], 1);
-    mbar_init(&bar_acc, p.dual ? 2 : 1);
+    mbar_init(&bar_acc, NM);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -204,17 +212,18 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
   if (tid == 0) pdl_launch_dependents();  // the next kernel may stage while this one runs
   const uint32_t tbase = tmem_base_sh;
   // TMEM columns: accumulators [1 or 2 MMA threads][FT][tn_cols], then A buffers [NA][FT][64]
-  const int nacc = p.dual ? 2 : 1;
+  constexpr int nacc = NM;
   auto acc_col = [&](int ft, int par) { return uint32_t((par * FT + ft) * p.tn_cols); };
   auto a_col = [&](int b, int ft) { return uint32_t(nacc * FT * p.tn_cols + (b * FT + ft) * 64); };
 
-  if (warp == 0) {
-    // ---------------- producer: step i's activation tile and weight tiles together ----------------
+  if (warp < NP) {
+    // ---------------- producers: step i's activation tile and weight tiles together ----------------
     // Both rings have the same depth and are refilled in lockstep: the SM's
     // copy engine serves requests in order, so an activation tile issued
     // later than the weight stream would wait behind many steps of weights.
     if (lane == 0) {
-      prefetch_tensormap(&x_map);
+      const int pw = warp;  // this producer issues the steps i with i % NP == pw
+      if (pw == 0) prefetch_tensormap(&x_map);
       const int S = XS;  // == WS
       auto issue_w = [&](int i) {  // one 8 KB bulk copy per feature tile, then the step's scales
         const int st = i % S, kt = kt_of(i);
@@ -229,10 +238,11 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
       // stream while it finishes (programmatic dependent launch); only a few,
       // so that the first activation tile does not queue behind many of them.
       const int pre = min(nk, min(S, 3));
-      for (int i = 0; i < pre; ++i) issue_w(i);
+      for (int i = pw; i < pre; i += NP) issue_w(i);
+
       pdl_wait();  // the activations are the previous kernel's output
       int issued_x = 0, issued_w = pre;
-      for (int i = 0; i < nk; ++i) {
+      for (int i = pw; i < nk; i += NP) {
         const int st = i % S, kt = kt_of(i);
         if (i >= S) {
           const uint32_t ph = ((i / S) - 1) & 1;
@@ -247,18 +257,20 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
           issued_w = i + 1;
         }
       }
-      if (abort_flag) {  // let the issued copies land before shared memory is released
+      if (abort_flag) {  // let this producer's issued copies land before shared memory is released
         for (int i = max(0, issued_x - S); i < issued_x; ++i) {
+          if (i % NP != pw) continue;
           uint32_t n = 0;
           while (!mbar_try_wait(&bar_x_full[i % S], (i / S) & 1) && ++n < kSleepLimit) {}
         }
         for (int i = max(0, issued_w - S); i < issued_w; ++i) {
+          if (i % NP != pw) continue;
           uint32_t n = 0;
           while (!mbar_try_wait(&bar_w_full[i % S], (i / S) & 1) && ++n < kSleepLimit) {}
         }
       }
     }
-  } else if (warp == 1 || (warp == 2 && p.dual)) {
+  } else if (warp < NP + NM) {
     // ---------------- MMA issuer(s) ----------------
     // With `dual`, warp 1 issues the even K steps into accumulator 0 and warp 2
     // the odd ones into accumulator 1, so one thread's barrier waits overlap the
@@ -270,7 +282,7 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
     // stage, i.e. that many 16-byte units added to the descriptor's address
     // field (bits 0-13, which these offsets never carry out of).
     if (lane == 0) {
-      const int par = warp - 1, stride = p.dual ? 2 : 1;
+      const int par = warp - NP, stride = NM;
       const uint32_t idesc = f16_idesc(0, 0, 0, 128, uint32_t(tn));
       const uint64_t xdesc0 = sw128_desc(smem_addr(sX(0)), 16, 1024);
       const uint32_t x_stage_units = uint32_t(x_bytes >> 4), kblk_units = uint32_t(tn * 8);
@@ -292,12 +304,12 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
       }
       mma_commit(&bar_acc);
     }
-  } else if (warp >= 3) {  // (warp 2 issues MMAs only in dual mode)
+  } else {
     // ---------------- dequantisation: thread = output feature, group = every other K step ----------------
     // Dequant warp dw: group gr = dw / (4 FT) takes the steps i with i % 2 == gr
     // (two steps in flight); inside a group, warp w -> feature tile (w / 4) % FT,
     // and the 4 warps of a tile cover the 4 TMEM lane quarters (warp & 3).
-    const int dw = (tid - 96) >> 5;
+    const int dw = (tid - 32 * (NP + NM)) >> 5;
     const int gr = dw / (4 * FT);
     const int ft = (dw >> 2) % FT;
     const int quarter = warp & 3;          // TMEM lanes this warp may access
@@ -308,7 +320,7 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
     // q - 8 = x - 1032 or x / 16 - 72, both exact in fp16 (constants 0x6408 =
     // 1032, 0x2C00 = 1/16, 0xD480 = -72).
     bool ok = true;
-    for (int i = gr; i < nk; i += 2) {
+    for (int i = gr; i < nk; i += NG) {
       const int st = i % WS, b = i % NA;
       ok = __all_sync(0xffffffffu, mbar_wait_sleep(&bar_w_full[st], (i / WS) & 1, &abort_flag, kSleepLimit));
       if (!ok) break;
@@ -369,12 +381,14 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
     if (ok) {
       tc_fence_after();
 #pragma unroll 1
-      for (int c4 = gr; c4 * 32 < tn; c4 += 2) {  // the two groups split the token columns
+      for (int c4 = gr; c4 * 32 < tn; c4 += NG) {  // the groups split the token columns
         uint32_t acc[32];
         tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft, 0) + c4 * 32, acc);
-        if (p.dual && nk > 1) {  // odd steps' accumulator (empty when there is one step)
+#pragma unroll 1
+        for (int par = 1; par < NM; ++par) {  // the other MMA warps' accumulators, in order
+          if (nk <= par) break;               // (a warp with no step wrote nothing)
           uint32_t acc1[32];
-          tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft, 1) + c4 * 32, acc1);
+          tmem_ld32(tbase + (uint32_t(quarter * 32) << 16) + acc_col(ft, par) + c4 * 32, acc1);
           tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c) acc[c] = __float_as_uint(__uint_as_float(acc[c]) + __uint_as_float(acc1[c]));
@@ -400,6 +414,45 @@ __global__ void __launch_bounds__(96 + FT * 256, CPS)
     tmem_dealloc(tbase, 512 / CPS);
   }
   if (tid == 0 && abort_flag) atomicExch(&g_w4a16_error, 1);
+  if constexpr (SPLIT) {
+    if (p.counters != nullptr) {
+      // Every CTA of the tile counts in (an aborted one too, so that the
+      // counter always returns to zero); the last one sums the splits' partials
+      // in split order (deterministic) and writes fp16, then resets the counter.
+      __shared__ int last_cta;
+      __threadfence();  // this thread's partial sums are visible device-wide
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t* cnt = p.counters + (int64_t(mblk) * gridDim.x + ftile);
+        const uint32_t prev = atomicAdd(cnt, 1u);
+        last_cta = prev + 1 == gridDim.z;
+        if (last_cta) *cnt = 0u;
+      }
+      __syncthreads();
+      if (last_cta) {
+        __threadfence();
+        const int rows = min(tn, p.M - mblk * tn);
+        constexpr int F4 = FT * 128 / 4;  // float4 columns of the tile
+        const int n_base = ftile * FT * 128;
+        const float* part = reinterpret_cast<const float*>(p.y);
+        for (int e = tid; e < rows * F4; e += blockDim.x) {
+          const int r = e / F4, c = e - r * F4;
+          const int64_t m = int64_t(mblk) * tn + r;
+          const int n0 = n_base + 4 * c;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int sp = 0; sp < int(gridDim.z); ++sp) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(part + (int64_t(sp) * p.M + m) * p.N + n0));
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+          }
+          const __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+          uint2 o;
+          o.x = *reinterpret_cast<const uint32_t*>(&lo);
+          o.y = *reinterpret_cast<const uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(p.y_out + m * p.y_out_stride + n0) = o;
+        }
+      }
+    }
+  }
 }
 
 }  // namespace
@@ -441,10 +494,15 @@ int sm_count() { return qa_sm_count(); }
 // Tile shape: FT feature tiles of 128 x tn tokens per CTA.
 struct GemmShape {
   int ft, tn, cps;  // feature tiles per CTA, tokens per CTA, CTAs per SM
+  int ng = 2, nm = 1, np = 1;  // dequant groups, MMA-issuing warps, producer warps
 };
 GemmShape gemm_shape(int M, int N) {
   const bool ft2 = N % 256 == 0;
-  if (M <= 64) return {1, ((M + 15) / 16) * 16, 2};
+  // M <= 64: one CTA per SM with four producer warps, four MMA warps (one
+  // accumulator each) and four dequant groups, i.e. four independent chains per
+  // role (measured against two CTAs per SM with two chains each: equal at M = 16,
+  // 1-8 % faster at M = 64, and one CTA per SM leaves TMEM for six A buffers)
+  if (M <= 64) return {1, ((M + 15) / 16) * 16, 1, 4, 4, 4};
   if (M <= 128) return {ft2 ? 2 : 1, ((M + 15) / 16) * 16, 1};
   if (M <= 256) return {1, ((M + 15) / 16) * 16, 1};
   // up to ~2K tokens two CTAs per SM overlap one CTA's prologue/epilogue with
@@ -496,9 +554,7 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   p.K = a.K;
   p.tn = sh.tn;
   p.tn_cols = ((sh.tn + 31) / 32) * 32;
-  // two MMA threads (one accumulator each) when their accumulators and >= 2 A buffers fit
-  p.dual = (512 / sh.cps - 2 * sh.ft * p.tn_cols) / (sh.ft * 64) >= 2 ? 1 : 0;
-  p.na = (512 / sh.cps - (p.dual ? 2 : 1) * sh.ft * p.tn_cols) / (sh.ft * 64);
+  p.na = (512 / sh.cps - sh.nm * sh.ft * p.tn_cols) / (sh.ft * 64);
   if (p.na > kMaxNA) p.na = kMaxNA;
   if (p.na < 2) return QA_ERR_UNSUPPORTED;
   const int w_stage = sh.ft * kWBytes + 1024;
@@ -512,11 +568,20 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   p.k_tiles_per_split = per;
   const dim3 grid{unsigned(a.N / (128 * sh.ft)), unsigned((a.M + sh.tn - 1) / sh.tn), unsigned(splits)};
   const bool split = splits > 1;
-  auto kern = sh.cps == 2 ? (split ? w4a16_gemm_kernel<1, true, 2> : w4a16_gemm_kernel<1, false, 2>)
-            : sh.ft == 2  ? (split ? w4a16_gemm_kernel<2, true, 1> : w4a16_gemm_kernel<2, false, 1>)
-                          : (split ? w4a16_gemm_kernel<1, true, 1> : w4a16_gemm_kernel<1, false, 1>);
+  using Kern = void (*)(CUtensorMap, GemmParams);
+  Kern kern = nullptr;
+#define QA_W4_PICK(FT_, CPS_, NG_, NM_, NP_)                                                     \
+  if (sh.ft == FT_ && sh.cps == CPS_ && sh.ng == NG_ && sh.nm == NM_ && sh.np == NP_)          \
+    kern = split ? w4a16_gemm_kernel<FT_, true, CPS_, NG_, NM_, NP_>                            \
+                 : w4a16_gemm_kernel<FT_, false, CPS_, NG_, NM_, NP_>;
+  QA_W4_PICK(1, 1, 4, 4, 4)
+  QA_W4_PICK(1, 2, 2, 1, 1)
+  QA_W4_PICK(2, 1, 2, 1, 1)
+  QA_W4_PICK(1, 1, 2, 1, 1)
+#undef QA_W4_PICK
+  if (kern == nullptr) return QA_ERR_UNSUPPORTED;
   if (qa_smem_attr(reinterpret_cast<const void*>(kern), smem) != cudaSuccess) return QA_ERR_LAUNCH;
-  const int threads = 96 + sh.ft * 256;
+  const int threads = 32 * (sh.np + sh.nm) + sh.ng * sh.ft * 128;
   // both kernels are launched as programmatic dependents of their predecessor
   cudaLaunchAttribute pdl[1];
   pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -528,7 +593,17 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   cfg.stream = st;
   cfg.attrs = pdl;
   cfg.numAttrs = 1;
-  if (split) {
+  p.counters = nullptr;
+  p.y_out = nullptr;
+  p.y_out_stride = 0;
+  if (split && a.counters != nullptr) {  // one launch: the last CTA of each tile reduces
+    p.y = a.workspace;
+    p.y_stride = a.N;
+    p.counters = a.counters;
+    p.y_out = reinterpret_cast<__half*>(a.y);
+    p.y_out_stride = a.y_stride;
+    if (cudaLaunchKernelEx(&cfg, kern, xm, p) != cudaSuccess) return QA_ERR_LAUNCH;
+  } else if (split) {
     p.y = a.workspace;
     p.y_stride = a.N;
     if (cudaLaunchKernelEx(&cfg, kern, xm, p) != cudaSuccess) return QA_ERR_LAUNCH;
@@ -619,8 +694,14 @@ namespace {
 constexpr int64_t kNoAllocScratchFloats = int64_t(4) << 20;  // 16 MiB of fp32 partial sums
 static __device__ __align__(256) float g_w4a16_scratch[kNoAllocScratchFloats];
 
+// split-K tile counters of the allocation-free entry point (zero at load; each
+// call leaves them zero)
+constexpr int kNoAllocCounters = 1 << 16;
+static __device__ __align__(256) uint32_t g_w4a16_counters[kNoAllocCounters];
+
 constexpr int kMaxDevices = 64;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
+uint32_t* g_counters_ptr[kMaxDevices] = {nullptr};
 
 // Device address of the scratch array for the current device. In host code the
 // array's name is only a host-side stand-in, so the address is looked up once
@@ -629,8 +710,10 @@ int scratch_for_current_device(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QA_ERR_DEVICE;
   if (g_scratch_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
+    void* ptr = nullptr, * cptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_w4a16_scratch) != cudaSuccess || ptr == nullptr) return QA_ERR_DEVICE;
+    if (cudaGetSymbolAddress(&cptr, g_w4a16_counters) != cudaSuccess || cptr == nullptr) return QA_ERR_DEVICE;
+    g_counters_ptr[dev] = static_cast<uint32_t*>(cptr);
     g_scratch_ptr[dev] = static_cast<float*>(ptr);
   }
   *out = g_scratch_ptr[dev];
@@ -666,6 +749,10 @@ extern "C" int qa_w4a16_gemm_noalloc(const qa_w4a16_args* args, void* stream) {
     const int st = scratch_for_current_device(&scratch);
     if (st != QA_OK) return st;
     a.workspace = scratch;  // every partial is written before it is read: nothing to clear
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t tiles = int64_t(a.N / 128) * ((a.M + 15) / 16);
+    a.counters = tiles <= kNoAllocCounters ? g_counters_ptr[dev] : nullptr;
   }
   a.splits = splits;
   return qa_w4a16_gemm(&a, stream);

@@ -149,6 +149,23 @@ def unpack_int4(qweight: torch.Tensor) -> torch.Tensor:
     return vals.reshape(N, K8 * 8).t().to(torch.int32).contiguous()
 
 
+_COUNTERS = {}
+
+
+def _split_counters(device, n: int):
+    """Zeroed split-K tile counters of a device (every GEMM leaves them zero), or None
+    when they would have to be created inside a CUDA-graph capture (that call then
+    adds its partials with a second kernel). Split-K GEMMs on one device share
+    them: do not run two at the same time on different streams."""
+    buf = _COUNTERS.get(device.index)
+    if buf is None or buf.numel() < n:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        buf = torch.zeros(max(n, 1 << 14), dtype=torch.int32, device=device)
+        _COUNTERS[device.index] = buf
+    return buf
+
+
 def w4a16_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
                  splits: int = 0, out: torch.Tensor = None) -> torch.Tensor:
     """``x @ dequant(qweight, scales)`` on the B200 tensor cores (fp16 in/out, fp32 accumulate).
@@ -181,7 +198,11 @@ def w4a16_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     a.workspace = ws.data_ptr() if ws is not None else None
     a.x_stride, a.y_stride = x2.stride(0), y.stride(0)
     a.M, a.N, a.K, a.splits = M, N, K, s.value
-    _lib.check(L.qa_w4a16_gemm(a, torch.cuda.current_stream(x.device).cuda_stream), "qa_w4a16_gemm")
+    stream = torch.cuda.current_stream(x.device)
+    if s.value > 1:  # split-K in one launch (the last CTA of each tile adds the partials)
+        cnt = _split_counters(x.device, (N // 128) * ((M + 15) // 16))
+        a.counters = cnt.data_ptr() if cnt is not None else None
+    _lib.check(L.qa_w4a16_gemm(a, stream.cuda_stream), "qa_w4a16_gemm")
     return y.view(*x.shape[:-1], N)
 
 
