@@ -1314,6 +1314,7 @@ int launch_tc_sub(TcParams& p, cudaStream_t st) {
 template <typename T, int D>
 int launch_tc_nbk(TcParams& p, cudaStream_t st) {
   if (p.kw_cap <= 32) return launch_tc_sub<T, D, 4>(p, st);
+  if (p.kw_cap <= 48) return launch_tc_sub<T, D, 6>(p, st);  // e.g. binary trees on subtree tiles
   if (p.kw_cap <= 64) return launch_tc_sub<T, D, 8>(p, st);
   return launch_tc_sub<T, D, 16>(p, st);
 }
