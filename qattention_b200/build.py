@@ -9,6 +9,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -30,7 +31,7 @@ def _headers() -> list[Path]:
 def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
     hdr_mtime = max((p.stat().st_mtime for p in _headers()), default=0.0)
-    objs = []
+    objs, cmds = [], []
     for src in sorted(CSRC.glob("*.cu")):
         obj = BUILD / (src.stem + ".o")
         objs.append(obj)
@@ -41,7 +42,11 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
             cmd += ["-Xptxas", "-v"]
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
+    # the translation units are independent: compile them side by side
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as pool:
+        for r in pool.map(lambda c: subprocess.run(c, check=True), cmds):
+            pass
     if not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart"]
         if verbose:

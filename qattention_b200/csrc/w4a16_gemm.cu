@@ -571,6 +571,14 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   p.tn_cols = ((sh.tn + 31) / 32) * 32;
   p.na = (512 / sh.cps - sh.nm * sh.ft * p.tn_cols) / (sh.ft * 64);
   if (p.na > kMaxNA) p.na = kMaxNA;
+  // Role chain c (producer, MMA warp or dequant group) handles the steps i
+  // with i % chains == c and waits on ring slots by phase parity, which cannot
+  // tell phase k from phase k + 2. Slot counts are therefore multiples of the
+  // chain count, so that a slot is only ever reused by the chain that used it
+  // last; otherwise a chain could pass its wait two phases early and overwrite
+  // a slot (or an A buffer) still in use.
+  const int chains = sh.np > sh.nm ? (sh.np > sh.ng ? sh.np : sh.ng) : (sh.nm > sh.ng ? sh.nm : sh.ng);
+  p.na -= p.na % chains;
   if (p.na < 2) return QA_ERR_UNSUPPORTED;
   const int w_stage = sh.ft * kWBytes + 1024;
   const int x_bytes = sh.tn * kBK * 2;
@@ -578,6 +586,7 @@ int w4a16_gemm_launch(const qa_w4a16_args& a, int splits, int per, cudaStream_t 
   const int smem = sh.cps == 2 ? kSmem2 : kSmem;
   int stages = (smem - 1024) / (x_bytes + w_stage);
   if (stages > kMaxXStages) stages = kMaxXStages;
+  stages -= stages % chains;
   if (stages < 2) return QA_ERR_UNSUPPORTED;
   p.x_stages = p.w_stages = stages;
   p.k_tiles_per_split = per;

@@ -29,6 +29,9 @@ def test_dequant_bit_exact(K, N):
 @pytest.mark.parametrize("M,N,K,splits", [
     (1, 128, 128, 1), (7, 256, 512, 0), (16, 256, 512, 1), (40, 256, 512, 2), (64, 384, 1024, 1), (65, 256, 512, 0), (128, 128, 4096, 0),
     (200, 512, 2048, 1), (200, 512, 2048, 4), (1024, 1024, 4096, 0), (33, 4096, 4096, 0),
+    # token counts whose shared-memory ring or TMEM buffer count is not a multiple of the
+    # kernel's chain count before rounding (ring slots must stay with one chain)
+    (16, 2048, 8192, 1), (80, 512, 8192, 1), (96, 512, 8192, 1), (112, 512, 8192, 1), (160, 256, 8192, 1),
 ])
 def test_gemm_vs_oracle(M, N, K, splits):
     qw, sc = _weights(K, N, M * 7 + N)
