@@ -727,17 +727,15 @@ def ancestor_sharded(cfg, ws, rank, dev, steps, warmup, clocks=None, with_e2e=Tr
            "local_bytes": local_bytes, "total_bytes": total_bytes, "trees_per_rank": sh.num_trees,
            "copies": copies}
     if with_e2e:
-        from qattention_b200 import sharding as shd
+        from qattention_b200.host_pipeline import ragged_attention_with_lse_host
         Qp, Kp, Vp = Qh.pin_memory(), Kh.pin_memory(), Vh.pin_memory()
         Op = torch.empty(sh.num_tokens, H, D, dtype=torch.float16).pin_memory()
         Lp = torch.empty(sh.num_tokens, H, dtype=torch.float32).pin_memory()
         e2e_steps = max(3, min(steps, 20))
 
         def e2e_step():
-            Qd, Kd, Vd = (x.to(dev, non_blocking=True) for x in (Qp, Kp, Vp))
-            Od, Ld = shd.sharded_ragged_attention_with_lse(Qd, Kd, Vd, sh, b, d)
-            Op.copy_(Od, non_blocking=True)
-            Lp.copy_(Ld, non_blocking=True)
+            if sh.num_trees:
+                ragged_attention_with_lse_host(Qp, Kp, Vp, sh.cu_local, b, d, device=dev, out=Op, lse_out=Lp)
 
         for _ in range(3):
             e2e_step()
@@ -753,8 +751,9 @@ def ancestor_sharded(cfg, ws, rank, dev, steps, warmup, clocks=None, with_e2e=Tr
         e2e_ms = _max_over_ranks(f0.elapsed_time(f1) / e2e_steps, ws)
         res["e2e"] = {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
                       "h2d_bytes_per_step": 3 * B * N * H * D * 2, "d2h_bytes_per_step": B * N * H * (2 * D + 4),
-                      "what": "each rank: H2D of its trees' Q/K/V from pinned memory, "
-                              "sharding.sharded_ragged_attention_with_lse, D2H of O and LSE; bytes summed over ranks"}
+                      "what": "each rank: host_pipeline.ragged_attention_with_lse_host on its trees' pinned "
+                              "Q/K/V (H2D, ancestor pass and D2H of O and LSE overlapped over chunks of "
+                              "whole trees on three streams); bytes summed over ranks"}
     if with_gather:
         if ws > 1:  # the first gather sets up NCCL's peer connections: warm them up untimed
             sharding.gather_outputs(O[:1], L[:1], sharding.shard_trees(

@@ -8,6 +8,7 @@ Kernels live in ``libqattn_b200.so`` (C ABI in ``include/qattn_b200.h``),
 built in-tree by ``python -m qattention_b200.build``.
 """
 from . import tree_mask  # noqa: F401
+from .host_pipeline import ragged_attention_with_lse_host  # noqa: F401
 from .ragged_attn import (  # noqa: F401
     build_paged_kv,
     fused_lse_merge,
