@@ -453,3 +453,31 @@ def test_paged_kv_rejects_unsupported():
         ra.ragged_attention_paged(Q, Kc, Kc, pt, cu, 0, 3)       # branching factor 0
     with pytest.raises(AssertionError):
         ra.ragged_attention_paged(Q, Kc, Kc[:, :8], pt, cu, 2, 3)
+
+
+def test_empty_sequences_and_empty_batch():
+    # zero-length sequences anywhere in the batch (the reference's grid returns early for
+    # rows past a sequence's length, src/ragged_attn.py:294-296) and a batch of no tokens
+    H, D, b, d = 4, 128, 2, 4
+    lens = [0, 31, 0, 0, 17, 31, 0]
+    g = torch.Generator().manual_seed(21)
+    qs, ks, vs = ([torch.randn(n, H, D, generator=g).half() for n in lens] for _ in range(3))
+    Q, K, V, cu = ra.pack_inputs(qs, ks, vs)
+    assert cu.tolist() == [0, 0, 31, 31, 31, 48, 79, 79]
+    O, L = ra.ragged_attention_with_lse(Q.cuda(), K.cuda(), V.cuda(), cu, b, d)
+    nz = [i for i, n in enumerate(lens) if n]
+    ref, rl = orc.padded_sdpa([qs[i] for i in nz], [ks[i] for i in nz], [vs[i] for i in nz],
+                              [orc.ancestor_mask(lens[i], b, d) for i in nz], return_lse=True)
+    assert torch.allclose(O.float().cpu(), torch.cat(ref, 0), atol=ATOL, rtol=RTOL)
+    assert torch.allclose(L.cpu(), torch.cat(rl, 0), atol=1e-3)
+    # the explicit-parent path on the same batch: BFS parents of the complete tree, per sequence
+    par = torch.cat([torch.tensor([max(0, (j - 1) // b) for j in range(n)], dtype=torch.int32) for n in lens])
+    Op, Lp = ra.ragged_attention_with_parents(Q.cuda(), K.cuda(), V.cuda(), cu, par.cuda(), d)
+    assert torch.allclose(Op.float().cpu(), torch.cat(ref, 0), atol=ATOL, rtol=RTOL)
+    assert torch.allclose(Lp.cpu(), torch.cat(rl, 0), atol=1e-3)
+    from qattention_b200 import _lib
+    assert _lib.ancestor_diagnostics()[0] == 0
+    # no tokens at all
+    E = torch.empty(0, H, D, dtype=torch.float16, device="cuda")
+    Oe, Le = ra.ragged_attention_with_lse(E, E, E, torch.tensor([0, 0], dtype=torch.int32), b, d)
+    assert Oe.shape == (0, H, D) and Le.shape == (0, H)
