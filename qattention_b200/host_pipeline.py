@@ -39,9 +39,10 @@ def chunk_bounds(cu: list, chunks: int) -> list:
     of near-equal token counts (boundary k = the tree start nearest k/chunks of the tokens)."""
     B = len(cu) - 1
     total = cu[-1]
+    n = max(1, min(chunks, B))  # fewer trees than chunks: one tree per chunk
     pts = [0]
-    for k in range(1, max(1, min(chunks, B))):
-        goal = total * k / chunks
+    for k in range(1, n):
+        goal = total * k / n
         j = next((i for i in range(B + 1) if cu[i] >= goal), B)
         if j > 0 and goal - cu[j - 1] < cu[j] - goal:
             j -= 1

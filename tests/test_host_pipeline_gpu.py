@@ -15,6 +15,7 @@ def test_chunk_bounds_cover_every_tree_once():
         assert len(pts) - 1 <= chunks
     assert chunk_bounds([0, 5, 100, 105], 2) == [0, 2, 3]  # cut nearest half of the tokens
     assert chunk_bounds([0, 7], 4) == [0, 1]
+    assert chunk_bounds([0, 1023, 2046], 8) == [0, 1, 2]  # two trees: two chunks, not one
 
 
 def _batch(lengths, H, D, dtype, seed):
