@@ -57,12 +57,12 @@ def _reference(model, tokens, cache0, L, b, d):
     return (x @ model.lm_head.float()).reshape(B * N, -1)
 
 
-@pytest.mark.parametrize("b,d,L", [(2, 3, 128), (4, 2, 200)])
-def test_verify_step_matches_fp32_model(b, d, L):
+@pytest.mark.parametrize("b,d,L,B", [(2, 3, 128, 2), (4, 2, 200, 2), (2, 3, 128, 1)])
+def test_verify_step_matches_fp32_model(b, d, L, B):
+    # B=1: one sequence per GPU, as config 5 runs when its 8 sequences are sharded over 8 GPUs
     cfg = vf.LlamaConfig(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000)
     model = vf.VerifyModel(cfg, "cuda", seed=3, std=0.05)
     N = (b ** (d + 1) - 1) // (b - 1)
-    B = 2
     cache = model.new_cache(B, L, N, seed=4)
     cache0 = [(k.clone(), v.clone()) for k, v in cache]
     tokens = torch.randint(0, cfg.vocab, (B, N), generator=torch.Generator().manual_seed(5)).cuda()
